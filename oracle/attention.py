@@ -1,0 +1,83 @@
+"""Paged decode / verify attention oracle (CPU, numpy).  Test infrastructure only.
+
+Restates ``paged_decode_attention_ref`` (reference
+``nanovllm/kernels/paged_decode_attn.py:472-495``): gather the pages of each
+sequence through its block table, upcast to float, softmax(q.K^T * scale).V per
+query head with GQA head sharing (``repeat_interleave``, :484-485), and emit
+zeros for a sequence whose cache length is 0 (:480-482).
+
+The k+1-row verify form follows flash-attn's ``flash_attn_varlen_func(...,
+causal=True, block_table=...)`` as called at ``nanovllm/layers/attention.py:67-70``
+with ``cu_seqlens_k`` = the cache length of each sequence
+(``nanovllm/engine/model_runner.py:531``): causal masking is aligned to the
+bottom-right corner, so query row r of n (r = 0..n-1) sees keys
+``j <= L - n + r``.  A row that sees no key (only possible when L < n) is zero,
+which is what flash-attn writes for a fully masked row.  With n = 1 this is
+exactly the decode oracle.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+
+def visible_keys(L: int, n: int, r: int) -> int:
+    """Number of keys query row ``r`` of ``n`` sees in a cache of length ``L``."""
+    return max(0, min(L, L - n + r + 1))
+
+
+def paged_attention(q, k_cache, v_cache, block_tables, cache_seqlens, scale,
+                    n_q: int = 1, compute_dtype=np.float32):
+    """Oracle for decode (n_q = 1) and speculative verify (n_q = k+1).
+
+    q            : (B*n_q, Hq, D)   rows of sequence b are b*n_q .. b*n_q+n_q-1
+    k_cache      : (NB, page, Hkv, D)
+    v_cache      : (NB, page, Hkv, D)
+    block_tables : (B, max_blocks) int32, -1 padded; only the first
+                   ceil(L/page) entries are read
+    cache_seqlens: (B,) int32, the cache length L of each sequence (it already
+                   includes the n_q new tokens in the verify step)
+    returns      : (B*n_q, Hq, D) in ``compute_dtype``
+    """
+    q = np.asarray(q)
+    k_cache = np.asarray(k_cache)
+    v_cache = np.asarray(v_cache)
+    block_tables = np.asarray(block_tables)
+    cache_seqlens = np.asarray(cache_seqlens)
+    total, Hq, D = q.shape
+    _, page, Hkv, _ = k_cache.shape
+    B = cache_seqlens.shape[0]
+    assert total == B * n_q, (total, B, n_q)
+    assert Hq % Hkv == 0
+    rep = Hq // Hkv
+    out = np.zeros((total, Hq, D), dtype=compute_dtype)
+    for b in range(B):
+        L = int(cache_seqlens[b])
+        if L <= 0:
+            continue                                   # zeros (paged_decode_attn.py:480-482)
+        nblk = (L + page - 1) // page
+        phys = block_tables[b, :nblk].astype(np.int64)
+        k = k_cache[phys].reshape(-1, Hkv, D)[:L].astype(compute_dtype)
+        v = v_cache[phys].reshape(-1, Hkv, D)[:L].astype(compute_dtype)
+        k = np.repeat(k, rep, axis=1)                  # (L, Hq, D), like repeat_interleave
+        v = np.repeat(v, rep, axis=1)
+        for r in range(n_q):
+            nv = visible_keys(L, n_q, r)
+            if nv == 0:
+                continue
+            qr = q[b * n_q + r].astype(compute_dtype)  # (Hq, D)
+            logits = np.einsum("hd,lhd->hl", qr, k[:nv]) * compute_dtype(scale)
+            logits = logits - logits.max(axis=-1, keepdims=True)
+            p = np.exp(logits)
+            p = p / p.sum(axis=-1, keepdims=True)
+            out[b * n_q + r] = np.einsum("hl,lhd->hd", p, v[:nv])
+    return out
+
+
+def algorithmic_bytes(cache_seqlens, n_q: int, Hq: int, Hkv: int, D: int,
+                      kv_elem: int, q_elem: int) -> int:
+    """Bytes a perfect kernel moves: every visible K/V row once plus q in and o out."""
+    L = np.asarray(cache_seqlens, dtype=np.int64)
+    kv = int(L.sum()) * 2 * Hkv * D * kv_elem
+    qo = 2 * L.shape[0] * n_q * Hq * D * q_elem
+    return kv + qo

@@ -1,0 +1,233 @@
+"""Generate the golden fixtures in this directory by running the REFERENCE's own Python code.
+
+Run once in a container that holds the reference checkout:
+
+    python tests/golden/make_golden.py --reference /path/to/specdec-nanovllm
+
+It loads three reference modules by file path (the same way the reference's
+own tests do, ``tests/test_spec_decode.py:14-26``), bypassing the package
+``__init__`` and its GPU-only imports:
+
+* ``nanovllm/kernels/paged_decode_attn.py`` -> ``paged_decode_attention_ref`` (:472)
+* ``nanovllm/layers/quant.py``              -> ``quantize_weight`` / ``dequantize_weight`` (:123, :151)
+* ``nanovllm/spec_decode/verify.py``        -> ``verify_batch`` (:42)
+
+``paged_decode_attn.py`` and ``quant.py`` import triton at module level; the
+Triton kernels are only defined there (``@triton.jit`` does not need a GPU), never
+launched.  ``verify_batch`` draws ``torch.rand`` (:120) and
+``Tensor.exponential_`` (:209) internally; both draws are replaced for the
+duration of each call by fixed tensors (Philox streams of ``oracle/philox.py``)
+that are saved with the case, so any implementation given the same draws must
+reproduce the same decisions and tokens.
+
+The fixtures are small ``.npz`` files; bf16 tensors are stored as uint16 bits.
+"""
+
+from __future__ import annotations
+
+import argparse
+import contextlib
+import importlib.util
+import os
+import sys
+
+import numpy as np
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REPO = os.path.dirname(os.path.dirname(HERE))
+sys.path.insert(0, REPO)
+
+from oracle import philox  # noqa: E402
+
+
+def _load(root, name, rel):
+    spec = importlib.util.spec_from_file_location(name, os.path.join(root, rel))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def bf16_bits(t: torch.Tensor) -> np.ndarray:
+    return t.contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+@contextlib.contextmanager
+def injected_draws(u: torch.Tensor, e: torch.Tensor):
+    """Replace the two random draws inside the reference's verify_batch."""
+    real_rand = torch.rand
+    real_exp = torch.Tensor.exponential_
+
+    def fake_rand(*size, **kw):
+        shape = size[0] if len(size) == 1 and isinstance(size[0], (tuple, list)) else size
+        assert tuple(shape) == tuple(u.shape), (shape, u.shape)
+        return u.clone().to(kw.get("dtype", torch.float32))
+
+    def fake_exp(self, lambd=1.0, **kw):
+        assert tuple(self.shape) == tuple(e.shape), (self.shape, e.shape)
+        self.copy_(e)
+        return self
+
+    torch.rand = fake_rand
+    torch.Tensor.exponential_ = fake_exp
+    try:
+        yield
+    finally:
+        torch.rand = real_rand
+        torch.Tensor.exponential_ = real_exp
+
+
+# ---------------------------------------------------------------------------
+def make_paged_inputs(g, B, Hq, Hkv, D, page, NB, max_blocks, lens, dtype):
+    lens = torch.tensor(lens, dtype=torch.int32)
+    bt = torch.full((B, max_blocks), -1, dtype=torch.int32)
+    perm = torch.randperm(NB, generator=g)
+    used = 0
+    for b in range(B):
+        nblk = (int(lens[b]) + page - 1) // page
+        bt[b, :nblk] = perm[used:used + nblk].to(torch.int32)
+        used += nblk
+    assert used <= NB
+    k = torch.randn(NB, page, Hkv, D, generator=g).to(dtype)
+    v = torch.randn(NB, page, Hkv, D, generator=g).to(dtype)
+    return k, v, bt, lens
+
+
+def attention_cases(ref, out_dir):
+    pda = ref["attn"]
+    g = torch.Generator().manual_seed(1234)
+    # --- decode, fp32, GQA 2 (the cfg1 path at a fixture-sized shape) -------------
+    B, Hq, Hkv, D, page, NB, mb = 5, 4, 2, 32, 16, 12, 4
+    lens = [0, 5, 16, 37, 64]
+    k, v, bt, cl = make_paged_inputs(g, B, Hq, Hkv, D, page, NB, mb, lens, torch.float32)
+    q = torch.randn(B, Hq, D, generator=g)
+    scale = D ** -0.5
+    o = pda.paged_decode_attention_ref(q, k, v, bt, cl, scale)
+    np.savez_compressed(os.path.join(out_dir, "attn_decode_fp32.npz"),
+                        q=q.numpy(), k_cache=k.numpy(), v_cache=v.numpy(),
+                        block_tables=bt.numpy(), cache_seqlens=cl.numpy(),
+                        scale=np.float32(scale), n_q=np.int32(1), out=o.numpy())
+
+    # --- decode + verify, bf16, GQA 4, head_dim 128 -------------------------------
+    B, Hq, Hkv, D, page, NB, mb = 5, 8, 2, 128, 64, 12, 4
+    lens = [0, 3, 64, 129, 250]
+    k, v, bt, cl = make_paged_inputs(g, B, Hq, Hkv, D, page, NB, mb, lens, torch.bfloat16)
+    scale = D ** -0.5
+    for n_q in (1, 4):
+        q = torch.randn(B * n_q, Hq, D, generator=g).to(torch.bfloat16)
+        # Verify rows are pinned through the reference's decode oracle: under
+        # flash-attn's bottom-right causal alignment, row r of n sees exactly the
+        # first L - n + r + 1 keys, i.e. it IS a decode with that cache length.
+        out_bf16 = torch.zeros(B * n_q, Hq, D, dtype=torch.bfloat16)
+        out_f32 = torch.zeros(B * n_q, Hq, D, dtype=torch.float32)
+        for r in range(n_q):
+            vis = torch.clamp(cl - n_q + r + 1, min=0).to(torch.int32)
+            vis = torch.minimum(vis, cl)
+            rows = torch.arange(B) * n_q + r
+            out_bf16[rows] = pda.paged_decode_attention_ref(q[rows], k, v, bt, vis, scale)
+            out_f32[rows] = pda.paged_decode_attention_ref(q[rows].float(), k.float(), v.float(),
+                                                           bt, vis, scale)
+        np.savez_compressed(os.path.join(out_dir, f"attn_bf16_nq{n_q}.npz"),
+                            q=bf16_bits(q), k_cache=bf16_bits(k), v_cache=bf16_bits(v),
+                            block_tables=bt.numpy(), cache_seqlens=cl.numpy(),
+                            scale=np.float32(scale), n_q=np.int32(n_q),
+                            out_bf16=bf16_bits(out_bf16), out_f32=out_f32.numpy())
+
+
+def quant_cases(ref, out_dir):
+    qm = ref["quant"]
+    g = torch.Generator().manual_seed(99)
+    N, K, M = 48, 256, 5
+    w = torch.randn(N, K, generator=g) * 0.05
+    w[3, 7] = 0.0
+    w[5] = 0.0                               # all-zero row: scale clamps to 1e-8
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16)
+    res = {"w": w.numpy(), "x": bf16_bits(x)}
+    for gran, gs in (("per_channel", 128), ("per_group", 64)):
+        q, s = qm.quantize_weight(w, gran, gs)
+        deq = qm.dequantize_weight(q, s, gran, gs)
+        y = x.float() @ deq.T
+        res[f"{gran}_q"] = q.numpy()
+        res[f"{gran}_scale"] = bf16_bits(s)
+        res[f"{gran}_deq"] = deq.numpy()
+        res[f"{gran}_y"] = y.numpy()
+    np.savez_compressed(os.path.join(out_dir, "quant.npz"), **res)
+
+
+def verify_cases(ref, out_dir):
+    vb = ref["verify"].verify_batch
+    g = torch.Generator().manual_seed(7)
+    cases = {}
+
+    def run(name, draft, target, tokens, temps=None, point=False, seed=0):
+        B, k, V = draft.shape
+        u = torch.from_numpy(philox.uniforms(seed, 0, B, k))
+        e = torch.from_numpy(philox.exponentials(seed, 0, B, V))
+        with injected_draws(u, e):
+            r = vb(draft, target, tokens, temps, draft_is_point_mass=point)
+        cases[name] = dict(draft=draft.numpy(), target=target.numpy(), tokens=tokens.numpy(),
+                           temps=(temps.numpy() if temps is not None else np.zeros(0, np.float32)),
+                           has_temps=np.bool_(temps is not None), point=np.bool_(point),
+                           seed=np.int64(seed), u=u.numpy(), e=e.numpy(),
+                           accepted=r.accepted.numpy(), bonus=r.bonus.numpy(),
+                           accept_mask=r.accept_mask.numpy())
+
+    def sample_tokens(logits):
+        B, k, V = logits.shape
+        pr = torch.softmax(logits, -1).reshape(B * k, V)
+        return torch.multinomial(pr, 1, generator=g).reshape(B, k)
+
+    # cfg4-like statistics at a small vocabulary
+    B, k, V = 8, 6, 997
+    target = torch.randn(B, k + 1, V, generator=g) * 3.0
+    draft = target[:, :k] + torch.randn(B, k, V, generator=g)
+    run("random", draft, target, sample_tokens(draft), seed=11)
+    temps = torch.tensor([0.5, 1.0, 2.0, 0.7, 1.3, 1.0, 3.0, 0.25])
+    run("temps", draft, target, sample_tokens(draft / temps[:, None, None]), temps=temps, seed=12)
+    # draft == target: everything accepted, bonus drawn from row k
+    t2 = torch.randn(4, 4, 300, generator=g) * 2.0
+    run("all_accept", t2[:, :3].clone(), t2, sample_tokens(t2[:, :3]), seed=13)
+    # point-mass draft (n-gram route)
+    B, k, V = 6, 3, 50
+    tgt = torch.randn(B, k + 1, V, generator=g) * 2.0
+    tok = torch.randint(0, V, (B, k), generator=g)
+    pm = torch.zeros(B, k, V)
+    pm.scatter_(2, tok.unsqueeze(-1), 1.0)
+    run("point_mass", pm, tgt, tok, point=True, seed=14)
+    # degenerate target with only k rows (no bonus row): p index clamps to k-1
+    tk = torch.randn(5, 3, 64, generator=g) * 2.0
+    dk = tk + torch.randn(5, 3, 64, generator=g)
+    run("k_rows_target", dk, tk, sample_tokens(dk), seed=15)
+    # the alignment case of the reference's test 6 (row j peaks at token 10+j)
+    K6, V6 = 3, 20
+    tl6 = torch.full((1, K6 + 1, V6), -30.0)
+    for j in range(K6 + 1):
+        tl6[0, j, 10 + j] = 30.0
+    run("align_all", tl6[:, :K6].clone(), tl6, torch.tensor([[10, 11, 12]]), seed=16)
+    dl7 = tl6[:, :K6].clone()
+    dl7[0, 0, 10] = -30.0
+    dl7[0, 0, 3] = 30.0
+    run("align_reject0", dl7, tl6.clone(), torch.tensor([[3, 11, 12]]), seed=17)
+    for name, c in cases.items():
+        np.savez_compressed(os.path.join(out_dir, f"verify_{name}.npz"), **c)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default=os.environ.get("SPECDEC_REFERENCE", "/root/reference"))
+    ap.add_argument("--out", default=HERE)
+    a = ap.parse_args()
+    ref = {
+        "attn": _load(a.reference, "ref_paged_decode_attn", "nanovllm/kernels/paged_decode_attn.py"),
+        "quant": _load(a.reference, "ref_quant", "nanovllm/layers/quant.py"),
+        "verify": _load(a.reference, "ref_verify", "nanovllm/spec_decode/verify.py"),
+    }
+    torch.manual_seed(0)
+    attention_cases(ref, a.out)
+    quant_cases(ref, a.out)
+    verify_cases(ref, a.out)
+    print("golden fixtures written to", a.out)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,81 @@
+"""Pin the CPU oracle to outputs of the reference's own code (fixtures in tests/golden/)."""
+
+import numpy as np
+import pytest
+
+from oracle import attention as oatt
+from oracle import philox
+from oracle import quant as oq
+from oracle import verify as ov
+from oracle.numerics import allclose_report, bf16_bits_to_f32, f32_to_bf16_bits
+
+
+def test_attention_decode_fp32_matches_reference(golden):
+    g = golden("attn_decode_fp32")
+    out = oatt.paged_attention(g["q"], g["k_cache"], g["v_cache"], g["block_tables"],
+                               g["cache_seqlens"], float(g["scale"]), n_q=1,
+                               compute_dtype=np.float64)
+    ok, err, _ = allclose_report(out, g["out"], rtol=1e-5, atol=1e-5)
+    assert ok, err
+    assert np.all(out[0] == 0)                       # L = 0 row is exactly zero
+
+
+@pytest.mark.parametrize("n_q", [1, 4])
+def test_attention_bf16_decode_and_verify_match_reference(golden, n_q):
+    g = golden(f"attn_bf16_nq{n_q}")
+    q = bf16_bits_to_f32(g["q"])
+    k = bf16_bits_to_f32(g["k_cache"])
+    v = bf16_bits_to_f32(g["v_cache"])
+    out = oatt.paged_attention(q, k, v, g["block_tables"], g["cache_seqlens"],
+                               float(g["scale"]), n_q=n_q, compute_dtype=np.float64)
+    ok, err, _ = allclose_report(out, g["out_f32"], rtol=1e-5, atol=1e-5)
+    assert ok, err
+    # The reference's bf16 output is its fp32 result rounded once to bf16.
+    ok, err, _ = allclose_report(bf16_bits_to_f32(f32_to_bf16_bits(out.astype(np.float32))),
+                                 bf16_bits_to_f32(g["out_bf16"]), rtol=1e-2, atol=1e-3)
+    assert ok, err
+
+
+def test_visible_keys_rule():
+    # bottom-right causal: last row sees everything, row r sees L-n+r+1 keys
+    assert [oatt.visible_keys(10, 4, r) for r in range(4)] == [7, 8, 9, 10]
+    assert [oatt.visible_keys(2, 4, r) for r in range(4)] == [0, 0, 1, 2]
+    assert oatt.visible_keys(0, 1, 0) == 0
+
+
+@pytest.mark.parametrize("gran,gs", [("per_channel", 128), ("per_group", 64)])
+def test_quantize_matches_reference(golden, gran, gs):
+    g = golden("quant")
+    q, s = oq.quantize_weight(g["w"], gran, gs)
+    assert np.array_equal(q, g[f"{gran}_q"])                       # bit-exact int8
+    assert np.array_equal(f32_to_bf16_bits(s), g[f"{gran}_scale"])  # bit-exact bf16 scale
+    deq = oq.dequantize_weight(q, s, gran, gs)
+    assert np.array_equal(deq, g[f"{gran}_deq"])
+    x = bf16_bits_to_f32(g["x"])
+    y = oq.int8_linear(x, q, s, granularity=gran, group_size=gs, dtype=np.float64)
+    ok, err, _ = allclose_report(y, g[f"{gran}_y"], rtol=1e-5, atol=1e-4)
+    assert ok, err
+
+
+VERIFY_CASES = ["random", "temps", "all_accept", "point_mass", "k_rows_target",
+                "align_all", "align_reject0"]
+
+
+@pytest.mark.parametrize("name", VERIFY_CASES)
+def test_verify_batch_matches_reference(golden, name):
+    g = golden("verify_" + name)
+    temps = g["temps"] if bool(g["has_temps"]) else None
+    r = ov.verify_batch(g["draft"], g["target"], g["tokens"], temps, bool(g["point"]),
+                        uniforms=g["u"], exponentials=g["e"])
+    assert np.array_equal(r.accepted, g["accepted"])
+    assert np.array_equal(r.accept_mask, g["accept_mask"])
+    assert np.array_equal(r.bonus, g["bonus"])
+
+
+def test_fixture_draws_are_the_philox_streams(golden):
+    g = golden("verify_random")
+    B, k = g["u"].shape
+    V = g["e"].shape[1]
+    seed = int(g["seed"])
+    assert np.array_equal(philox.uniforms(seed, 0, B, k), g["u"])
+    assert np.array_equal(philox.exponentials(seed, 0, B, V), g["e"])
