@@ -1,0 +1,371 @@
+"""Benchmark of the speculative-verify attention hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...        (one process per GPU)
+
+Workload (BASELINE configuration 2 at its target point): paged verify attention,
+Qwen3-4B shapes (32 q / 8 kv heads, head_dim 128), k = 6 (7 causal query rows per
+sequence), 64 sequences of 4096 cached tokens per GPU, page 256, scattered block
+tables, bf16, synthetic N(0,1) data.  A step is one kernel pass over the batch.
+Multi-GPU runs shard sequences: every rank owns its own 64 sequences and KV pool
+(weak scaling, no collective on the data path).
+
+Metric: HBM GB/s of algorithmic bytes (every visible K/V row once + q in + o out)
+per second, summed over ranks, timed with CUDA events (max over ranks).  One JSON
+line on rank 0.  ``--impl reference`` times the reference's CPU algorithm (the
+oracle restatement of ``paged_decode_attention_ref``) on this host's cores.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import importlib.util
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+B_PER_GPU, CTX, K_SPEC, PAGE = 64, 4096, 6, 256
+HQ, HKV, D = 32, 8, 128
+N_Q = K_SPEC + 1
+METRIC = "verify-attn HBM GB/s (% of 8 TB/s)"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def load_package():
+    name = "specdec_nanovllm_b200"
+    if name in sys.modules:
+        return sys.modules[name]
+    pkg_dir = os.path.join(ROOT, "specdec-nanovllm_b200")
+    spec = importlib.util.spec_from_file_location(name, os.path.join(pkg_dir, "__init__.py"),
+                                                  submodule_search_locations=[pkg_dir])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def measured_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def committed_traffic(workload: str):
+    """dram bytes per launch from the committed ncu summary (profiles/traffic.json)."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            return json.load(f).get(workload)
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.dev = device_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", str(self.dev), "-lms", "100"], stdout=subprocess.PIPE,
+                stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# --------------------------------------------------------------------------- CPU legs
+def cpu_threads() -> int:
+    try:
+        from threadpoolctl import threadpool_info
+        n = [i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"]
+        return max(n) if n else 1
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def cpu_inputs(seed: int = 0, n_seqs: int = 2):
+    """A host copy of a few sequences of the workload (bf16 values held as float32)."""
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    nblk = CTX // PAGE
+    nb = n_seqs * nblk
+    k = rng.standard_normal((nb, PAGE, HKV, D), dtype=np.float32)
+    v = rng.standard_normal((nb, PAGE, HKV, D), dtype=np.float32)
+    q = rng.standard_normal((n_seqs * N_Q, HQ, D), dtype=np.float32)
+    bt = rng.permutation(nb).astype(np.int32).reshape(n_seqs, nblk)
+    cl = np.full((n_seqs,), CTX, dtype=np.int32)
+    return q, k, v, bt, cl
+
+
+def time_cpu_reference(budget_s: float, steps: int = 1):
+    """Time the oracle restatement of the reference CPU path on (sequence, kv head) pairs.
+
+    Returns (GB/s of algorithmic bytes, seconds, pairs per step, description)."""
+    from oracle import attention as oatt
+    q, k, v, bt, cl = cpu_inputs()
+    pairs_all = [(b, h) for b in range(q.shape[0] // N_Q) for h in range(HKV)]
+    oatt.paged_attention_pairs(q, k, v, bt, cl, D ** -0.5, N_Q, pairs_all[:1])      # warm-up
+    t0 = time.perf_counter()
+    oatt.paged_attention_pairs(q, k, v, bt, cl, D ** -0.5, N_Q, pairs_all[:2])
+    per_pair = max((time.perf_counter() - t0) / 2, 1e-4)
+    n_pairs = max(1, min(len(pairs_all), int(budget_s / max(steps, 1) / per_pair)))
+    pairs = [pairs_all[i % len(pairs_all)] for i in range(n_pairs)]
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        oatt.paged_attention_pairs(q, k, v, bt, cl, D ** -0.5, N_Q, pairs)
+        times.append(time.perf_counter() - t0)
+    bytes_per_pair = CTX * 2 * D * 2 + 2 * N_Q * (HQ // HKV) * D * 2   # bf16 K/V rows + q + o
+    gbs = n_pairs * bytes_per_pair / statistics.median(times) / 1e9
+    desc = (f"{n_pairs} (sequence, kv head) pairs of the workload per step (ctx {CTX}, {N_Q} rows, "
+            f"GQA 4), numpy float32 + BLAS, median of {steps}")
+    return gbs, sum(times), n_pairs, desc
+
+
+# --------------------------------------------------------------------------- reference arm
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    budget = 150.0
+    total_steps = args.steps + args.warmup
+    per_step_budget = max(0.05, budget / max(total_steps, 1))
+    from oracle import attention as oatt
+    q, k, v, bt, cl = cpu_inputs()
+    pairs_all = [(b, h) for b in range(q.shape[0] // N_Q) for h in range(HKV)]
+    oatt.paged_attention_pairs(q, k, v, bt, cl, D ** -0.5, N_Q, pairs_all[:1])
+    t0 = time.perf_counter()
+    oatt.paged_attention_pairs(q, k, v, bt, cl, D ** -0.5, N_Q, pairs_all[:2])
+    per_pair = max((time.perf_counter() - t0) / 2, 1e-4)
+    n_pairs = max(1, min(len(pairs_all), int(per_step_budget / per_pair)))
+    pairs = [pairs_all[i % len(pairs_all)] for i in range(n_pairs)]
+    for _ in range(args.warmup):
+        oatt.paged_attention_pairs(q, k, v, bt, cl, D ** -0.5, N_Q, pairs)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oatt.paged_attention_pairs(q, k, v, bt, cl, D ** -0.5, N_Q, pairs)
+    dt = time.perf_counter() - t0
+    bytes_per_pair = CTX * 2 * D * 2 + 2 * N_Q * (HQ // HKV) * D * 2
+    gbs = n_pairs * bytes_per_pair * args.steps / dt / 1e9
+    threads = cpu_threads()
+    sample = (f"{n_pairs} (sequence, kv head) pairs per step of the verify workload (ctx {CTX}, "
+              f"k={K_SPEC}, GQA 4); oracle restatement of paged_decode_attention_ref extended to "
+              f"k+1 causal rows, numpy float32 + BLAS")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(dt / max(args.steps, 1) * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"verify-attn B={B_PER_GPU}/GPU ctx={CTX} k={K_SPEC} Qwen3-4B heads",
+                   "global_batch": B_PER_GPU * args.gpus, "seq_len": CTX, "parallelism": "host cores"},
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# --------------------------------------------------------------------------- our arm
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    pkg = load_package()
+    from specdec_nanovllm_b200 import workloads
+    from oracle.attention import algorithmic_bytes
+
+    case = workloads.paged_case([CTX] * B_PER_GPU, N_Q, Hq=HQ, Hkv=HKV, D=D, page=PAGE,
+                                dtype=torch.bfloat16, device=dev, seed=1000 + rank,
+                                extra_blocks=0, generate_on_device=True)
+    bytes_per_step = algorithmic_bytes([CTX] * B_PER_GPU, N_Q, HQ, HKV, D, 2, 2)
+    out = torch.empty_like(case.q)
+
+    def step():
+        pkg.paged_attention(case.q, case.k_cache, case.v_cache, case.block_tables, case.cache_seqlens,
+                            case.scale, n_q=N_Q, out=out)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    sampler = ClockSampler(dev.index)
+    sampler.start()
+    time.sleep(0.3)  # the sampler's first reading lands inside the timed region
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    ev0.record()
+    for _ in range(args.steps):
+        step()
+    ev1.record()
+    barrier()
+    clocks = sampler.stop()
+    ms = max_over_ranks(ev0.elapsed_time(ev1))
+    ms_step = ms / args.steps
+    value = bytes_per_step * world / (ms_step * 1e-3) / 1e9
+
+    # ---- e2e: the public call with pinned host buffers, copies inside the timed region
+    q_h = case.q.cpu().pin_memory()
+    bt_h = case.block_tables.cpu().pin_memory()
+    cl_h = case.cache_seqlens.cpu().pin_memory()
+    out_h = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+    q_d = torch.empty_like(case.q)
+    bt_d = torch.empty_like(case.block_tables)
+    cl_d = torch.empty_like(case.cache_seqlens)
+
+    def e2e_step():
+        q_d.copy_(q_h, non_blocking=True)
+        bt_d.copy_(bt_h, non_blocking=True)
+        cl_d.copy_(cl_h, non_blocking=True)
+        pkg.paged_attention(q_d, case.k_cache, case.v_cache, bt_d, cl_d, case.scale, n_q=N_Q, out=out)
+        out_h.copy_(out, non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record()
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
+    e2e_val = bytes_per_step * world / (e2e_ms * 1e-3) / 1e9
+    h2d = q_h.numel() * q_h.element_size() + bt_h.numel() * 4 + cl_h.numel() * 4
+    d2h = out_h.numel() * out_h.element_size()
+
+    # ---- memory-floor twin (same grid and TMA stream, no math), outside the timed region
+    ro_ws = pkg.paged_attention_readonly(case.q, case.k_cache, case.v_cache, case.block_tables,
+                                         case.cache_seqlens, n_q=N_Q)
+    r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n_ro = max(10, min(args.steps, 200))
+    r0.record()
+    for _ in range(n_ro):
+        pkg.paged_attention_readonly(case.q, case.k_cache, case.v_cache, case.block_tables,
+                                     case.cache_seqlens, n_q=N_Q, workspace=ro_ws)
+    r1.record()
+    torch.cuda.synchronize()
+    kv_bytes = CTX * B_PER_GPU * 2 * HKV * D * 2
+    ro_gbs = kv_bytes / (r0.elapsed_time(r1) / n_ro * 1e-3) / 1e9
+
+    peak, peak_kind = measured_peak()
+    per_launch_gbs = bytes_per_step / (ms_step * 1e-3) / 1e9
+    workload = f"verify-attn B={B_PER_GPU} ctx={CTX} k={K_SPEC}"
+    traffic = committed_traffic(workload)
+    splits = pkg.attention.default_splits(B_PER_GPU, N_Q, HQ, HKV, D, PAGE, CTX // PAGE, torch.bfloat16)
+
+    cpu = None
+    if world == 1 and rank == 0 and not args.skip_cpu:
+        gbs, secs, n_pairs, desc = time_cpu_reference(budget_s=12.0, steps=3)
+        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": cpu_threads(), "kind": "port",
+               "sample": desc}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": f"{workload} (Qwen3-4B heads 32/8, head_dim 128, page {PAGE}) per GPU",
+                       "global_batch": B_PER_GPU * world, "seq_len": CTX, "k": K_SPEC,
+                       "parallelism": f"seq-shard{world}", "splits": splits,
+                       "l2": "no flush: 1.07 GB of KV per GPU per step exceeds the 126 MB L2",
+                       "bytes_per_step_per_gpu": bytes_per_step},
+            "pct_of_8tbs": round(100.0 * per_launch_gbs / 8000.0, 2),
+            "roofline": {"bound": "hbm", "achieved": round(per_launch_gbs, 2), "peak": peak,
+                         "peak_kind": peak_kind, "unit": "GB/s",
+                         "frac": round(per_launch_gbs / peak, 4),
+                         "traffic": traffic, "kernel": "pa_mma_kernel",
+                         "readonly_floor_gbs": round(ro_gbs, 2)},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 5)},
+            "gpu_launches": args.steps,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=4000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--skip-cpu", action="store_true", help="omit the CPU baseline leg")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,196 @@
+/*
+ * specdec_b200.h -- C ABI of the B200 (sm_100a) decode / speculative-verify hot path.
+ *
+ * Every entry point takes plain device pointers, element strides and sizes, a
+ * caller-owned workspace and a cudaStream_t (passed as void*), launches on that
+ * stream, allocates nothing, never synchronises the device and returns a status
+ * code (SDB_OK or one of SDB_ERR_*), so every call can be captured in a CUDA
+ * graph.  Tensor layouts are the reference's (henry-tmp-de/specdec-nanovllm).
+ *
+ * Thread safety: calls are re-entrant across streams as long as concurrent calls
+ * use distinct workspaces.
+ */
+#ifndef SPECDEC_B200_H
+#define SPECDEC_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes -------------------------------------------------------- */
+#define SDB_OK                 0
+#define SDB_ERR_INVALID_ARG    1   /* null pointer, negative size, bad stride      */
+#define SDB_ERR_UNSUPPORTED    2   /* shape / dtype combination not built          */
+#define SDB_ERR_WORKSPACE      3   /* workspace missing or too small               */
+#define SDB_ERR_CUDA           4   /* launch or driver error (see sdb_last_error)  */
+
+/* Bits a kernel ORs into the workspace error word (sdb_*_error_word). */
+#define SDB_KERR_SEQLEN        0x1 /* cache length < 0 or > max_blocks * page      */
+#define SDB_KERR_BLOCK_ID      0x2 /* block table entry outside [0, num_blocks)    */
+#define SDB_KERR_TIMEOUT       0x4 /* a bounded wait gave up                       */
+#define SDB_KERR_TOKEN         0x8 /* draft token outside [0, vocab)               */
+
+/* ---- dtypes --------------------------------------------------------------- */
+#define SDB_F32   0
+#define SDB_BF16  1
+#define SDB_F16   2
+
+/* Human-readable message of the last SDB_ERR_CUDA on this thread. */
+const char* sdb_last_error(void);
+
+/* Library build identity: "sm_100a" and the list of kernels compiled in. */
+const char* sdb_build_info(void);
+
+/* =========================================================================
+ * Paged decode / verify attention.
+ *
+ * Replaces, with one kernel family:
+ *   - flash_attn_with_kvcache(q, k_cache, v_cache, cache_seqlens, block_table,
+ *     softmax_scale, causal=True)           nanovllm/layers/attention.py:78-81 (decode, n_q = 1)
+ *   - flash_attn_varlen_func(q, k_cache, v_cache, cu_seqlens_q, cu_seqlens_k, ...,
+ *     causal=True, block_table)              nanovllm/layers/attention.py:67-70 (verify, n_q = k+1)
+ *   - paged_decode_attention / paged_decode_attention_cuda
+ *                                            nanovllm/kernels/paged_decode_attn.py:352,
+ *                                            nanovllm/kernels/paged_decode_attn_cuda.py:52
+ *
+ *   q       (B*n_q, Hq, D)          rows b*n_q .. b*n_q+n_q-1 belong to sequence b
+ *   k_cache (num_blocks, page, Hkv, D)  the nano-vllm / flash-attn paged layout
+ *   v_cache same layout (may alias a different base with the same strides)
+ *   block_tables (B, max_blocks) int32, -1 padded; only the first ceil(L/page)
+ *                entries of a row are read
+ *   cache_seqlens (B) int32 L_b: keys in the cache, the n_q new ones included
+ *   out     (B*n_q, Hq, D)          same dtype as q
+ *
+ * Row r (0..n_q-1) of sequence b attends to keys j <= L_b - n_q + r (flash-attn's
+ * bottom-right causal alignment); rows that see no key, and every row of an
+ * L_b = 0 sequence, are written as zeros.  Strides are in elements; the last dim
+ * of q / out / caches must be contiguous.
+ *
+ * dtype: SDB_BF16 / SDB_F16 (tensor-core path: D = 128, page % 64 == 0,
+ *        n_q*Hq/Hkv <= 64) or SDB_F32 (CUDA-core path, fp32 accumulate, any
+ *        page, D in {64, 128, 256}, n_q*Hq/Hkv <= 32).
+ * splits: KV splits per (sequence, kv head); 0 picks a default from the static
+ *         shape (max_blocks * page), never from device data.
+ * workspace: sdb_paged_attention_workspace_size() bytes, 256-byte aligned,
+ *         zero-filled once before first use (the kernels leave it re-usable).
+ * ========================================================================= */
+size_t sdb_paged_attention_workspace_size(int B, int n_q, int Hq, int Hkv, int D, int splits);
+
+int sdb_paged_attention_default_splits(int B, int n_q, int Hq, int Hkv, int D, int page,
+                                       int max_blocks, int dtype);
+
+int sdb_paged_attention(const void* q, int64_t q_stride_row, int64_t q_stride_head,
+                        const void* k_cache, const void* v_cache,
+                        int64_t kv_stride_block, int64_t kv_stride_page, int64_t kv_stride_head,
+                        const int32_t* block_tables, int64_t bt_stride,
+                        const int32_t* cache_seqlens,
+                        void* out, int64_t o_stride_row, int64_t o_stride_head,
+                        int B, int n_q, int Hq, int Hkv, int D, int page,
+                        int max_blocks, int num_blocks,
+                        float softmax_scale, int dtype, int splits,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+/* Memory-floor twin of sdb_paged_attention: the same grid, the same TMA loads
+ * of every visible K/V tile, no math; writes one checksum word per CTA into the
+ * workspace.  Reference counterpart: paged_decode_readonly_kernel,
+ * nanovllm/kernels/paged_decode_attn_cuda.cu:654-705. */
+int sdb_paged_attention_readonly(const void* q, int64_t q_stride_row, int64_t q_stride_head,
+                                 const void* k_cache, const void* v_cache,
+                                 int64_t kv_stride_block, int64_t kv_stride_page,
+                                 int64_t kv_stride_head,
+                                 const int32_t* block_tables, int64_t bt_stride,
+                                 const int32_t* cache_seqlens,
+                                 int B, int n_q, int Hq, int Hkv, int D, int page,
+                                 int max_blocks, int num_blocks, int dtype, int splits,
+                                 void* workspace, size_t workspace_bytes, void* stream);
+
+/* Error word the attention kernels OR SDB_KERR_* bits into (device pointer
+ * inside the workspace; read it after a synchronise when debugging). */
+const int32_t* sdb_paged_attention_error_word(const void* workspace, int B, int n_q, int Hq,
+                                              int Hkv, int D, int splits);
+
+
+/* store_kvcache: scatter the new K/V rows of this step into the paged cache.
+ * Replaces store_kvcache / store_kvcache_kernel   nanovllm/layers/attention.py:10-40.
+ *   key, value (N, Hkv, D); slot_mapping (N) int32, slot = block * page + offset,
+ *   -1 = skip the row (graph padding).  workspace: the attention workspace (its
+ *   error word records slots past num_blocks). */
+int sdb_store_kvcache(const void* key, int64_t key_stride_tok, int64_t key_stride_head,
+                      const void* value, int64_t value_stride_tok, int64_t value_stride_head,
+                      void* k_cache, void* v_cache,
+                      int64_t kv_stride_block, int64_t kv_stride_page, int64_t kv_stride_head,
+                      const int32_t* slot_mapping, int N, int Hkv, int D, int page, int num_blocks,
+                      int dtype, void* workspace, void* stream);
+
+/* =========================================================================
+ * verify_batch: lossless rejection sampling of k drafted tokens.
+ *
+ * Replaces verify_batch(draft_probs, target_logits, draft_tokens, temperatures,
+ * draft_is_point_mass) -> VerifyResult      nanovllm/spec_decode/verify.py:42-175
+ *
+ *   draft_logits  (B, k, V) float32  raw draft logits (or probabilities when
+ *                 draft_is_point_mass != 0, used as-is, verify.py:86-87)
+ *   target_logits (B, target_rows, V) float32, target_rows = k+1 (or k)
+ *   draft_tokens  (B, k) int64
+ *   temperatures  (B) float32 or NULL (no division)
+ *   uniforms      (B, k) float32 or NULL: acceptance draws; NULL -> Philox
+ *                 stream 0 keyed by (seed, offset)
+ *   exponentials  (B, V) float32 or NULL: bonus Exp(1) draws; NULL -> Philox
+ *                 stream 1 keyed by (seed, offset)
+ *   out_accepted  (B) int64, out_bonus (B) int64, out_accept_mask (B, k) uint8
+ *   workspace     sdb_verify_workspace_size() bytes, zero-filled once.
+ * ========================================================================= */
+size_t sdb_verify_workspace_size(int B, int k, int target_rows, int V);
+
+int sdb_verify_batch(const float* draft_logits, const float* target_logits,
+                     const int64_t* draft_tokens, const float* temperatures,
+                     const float* uniforms, const float* exponentials,
+                     uint64_t seed, uint64_t offset, int draft_is_point_mass,
+                     int64_t* out_accepted, int64_t* out_bonus, uint8_t* out_accept_mask,
+                     int B, int k, int target_rows, int V,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
+/* Philox streams of the sampler written out (test and debugging aid): stream 0
+ * as uniforms [rows, cols] or stream 1 as exponentials [rows, cols]. */
+int sdb_philox_fill(float* out, int rows, int cols, uint64_t seed, uint64_t offset,
+                    int stream_id, void* stream);
+
+/* =========================================================================
+ * W8A16 linear: y = x @ (q * scale)^T (+ bias), int8 weights dequantised in
+ * registers.
+ *
+ * Replaces int8_linear(x, qweight, scale, bias, granularity, group_size)
+ *                                           nanovllm/layers/quant.py:262-310
+ *
+ *   x     (M, K) act_dtype (SDB_BF16 or SDB_F16), rows contiguous, x_stride_row
+ *   qweight (N, K) int8 row-major (K contiguous)
+ *   scale (N) per output channel (group_size == 0) or (N, K/group_size),
+ *         scale_dtype SDB_BF16 / SDB_F16 / SDB_F32
+ *   bias  (N) act_dtype or NULL
+ *   y     (M, N) act_dtype, y_stride_row
+ *   Requires K % 64 == 0; group_size 0 or a multiple of 64 dividing K.
+ *   workspace: sdb_w8a16_workspace_size() bytes (split-K partials), zero-filled once.
+ * ========================================================================= */
+size_t sdb_w8a16_workspace_size(int M, int N, int K);
+
+int sdb_w8a16_linear(const void* x, int64_t x_stride_row, const int8_t* qweight,
+                     const void* scale, int scale_dtype, int group_size,
+                     const void* bias, void* y, int64_t y_stride_row,
+                     int M, int N, int K, int act_dtype,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
+/* quantize_weight: symmetric int8 quantisation of a (N, K) weight.
+ * Replaces quantize_weight(w, granularity, group_size)  nanovllm/layers/quant.py:123-148.
+ * w float32/bf16/f16 (w_dtype), q out int8 (N, K), scale out (N) or (N, K/G) in
+ * scale_dtype (the scale is computed in float32 and rounded once, as the reference). */
+int sdb_quantize_weight(const void* w, int w_dtype, int8_t* q, void* scale, int scale_dtype,
+                        int N, int K, int group_size, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SPECDEC_B200_H */

@@ -81,3 +81,37 @@ def algorithmic_bytes(cache_seqlens, n_q: int, Hq: int, Hkv: int, D: int,
     kv = int(L.sum()) * 2 * Hkv * D * kv_elem
     qo = 2 * L.shape[0] * n_q * Hq * D * q_elem
     return kv + qo
+
+
+def paged_attention_pairs(q, k_cache, v_cache, block_tables, cache_seqlens, scale, n_q, pairs):
+    """The same computation restricted to a list of (sequence, kv head) pairs, in float32
+    with batched matmuls (the timed CPU baseline: the reference's
+    ``paged_decode_attention_ref`` math, one GQA group at a time).
+
+    Returns {(b, kvh): (n_q, G, D) float32}.
+    """
+    total, Hq, D = q.shape
+    _, page, Hkv, _ = k_cache.shape
+    G = Hq // Hkv
+    out = {}
+    for b, h in pairs:
+        L = int(cache_seqlens[b])
+        res = np.zeros((n_q, G, D), dtype=np.float32)
+        if L > 0:
+            nblk = (L + page - 1) // page
+            phys = block_tables[b, :nblk].astype(np.int64)
+            k = k_cache[phys, :, h].reshape(-1, D)[:L].astype(np.float32)     # (L, D)
+            v = v_cache[phys, :, h].reshape(-1, D)[:L].astype(np.float32)
+            qg = q[b * n_q:(b + 1) * n_q, h * G:(h + 1) * G].astype(np.float32)  # (n_q, G, D)
+            logits = (qg.reshape(n_q * G, D) @ k.T).reshape(n_q, G, L) * np.float32(scale)
+            for r in range(n_q):
+                nv = visible_keys(L, n_q, r)
+                if nv == 0:
+                    continue
+                lg = logits[r, :, :nv]
+                lg = lg - lg.max(axis=-1, keepdims=True)
+                p = np.exp(lg)
+                p /= p.sum(axis=-1, keepdims=True)
+                res[r] = p @ v[:nv]
+        out[(b, h)] = res
+    return out

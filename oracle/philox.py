@@ -89,10 +89,16 @@ def words_to_open_uniform(w) -> np.ndarray:
             * np.float32(2.0 ** -24))
 
 
-_SQRT2 = np.float32(1.41421356)
-_LN2_HI = np.float32(0.693145751953125)      # 12 significant bits: e*LN2_HI is exact
-_LN2_LO = np.float32(1.428606765330187e-06)  # ln 2 - LN2_HI
-_C = [np.float32(1.0 / d) for d in (11.0, 9.0, 7.0, 5.0, 3.0)]
+def _f32(bits: int) -> np.float32:
+    return np.array([bits], dtype=np.uint32).view(np.float32)[0]
+
+
+# Constants by bit pattern so no decimal-to-binary rounding can differ between
+# numpy and nvcc.
+_SQRT2 = _f32(0x3FB504F3)   # sqrt(2) rounded to float32
+_LN2_HI = _f32(0x3F317200)  # 0.693145751953125, 16 significant bits: e*LN2_HI is exact
+_LN2_LO = _f32(0x35BFBE8E)  # ln 2 - LN2_HI
+_C = [_f32(b) for b in (0x3DBA2E8C, 0x3DE38E39, 0x3E124925, 0x3E4CCCCD, 0x3EAAAAAB)]  # 1/11 1/9 1/7 1/5 1/3
 
 
 def log_f32(x) -> np.ndarray:

@@ -1,0 +1,105 @@
+// Host-side plumbing shared by every entry point: status strings, device
+// queries, the once-per-device shared-memory opt-in and the tensor-map encoder.
+#include <cudaTypedefs.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "common.cuh"
+
+namespace sdb {
+
+static thread_local char g_last_error[512] = "no error";
+
+void set_last_error(const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+    va_end(ap);
+}
+
+int cuda_status(cudaError_t e, const char* where) {
+    if (e == cudaSuccess) return SDB_OK;
+    set_last_error("%s: %s (%s)", where, cudaGetErrorName(e), cudaGetErrorString(e));
+    return SDB_ERR_CUDA;
+}
+
+int device_index() {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    return dev;
+}
+
+int device_sm_count() {
+    static int cache[64] = {0};
+    const int dev = device_index();
+    if (dev < 0 || dev >= 64) return 148;
+    if (cache[dev] == 0) {
+        int n = 0;
+        if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+            n = 148;
+        cache[dev] = n;
+    }
+    return cache[dev];
+}
+
+int ensure_smem_attr(const void* func, int bytes, int slot) {
+    // slot identifies the kernel instantiation; one opt-in per (device, slot).
+    constexpr int kSlots = 128;
+    static int done[64][kSlots] = {{0}};
+    static std::mutex mu;
+    const int dev = device_index();
+    if (slot < 0 || slot >= kSlots || dev < 0 || dev >= 64) {
+        return cuda_status(cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes),
+                           "cudaFuncSetAttribute");
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    if (done[dev][slot] >= bytes) return SDB_OK;
+    int st = cuda_status(cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes),
+                         "cudaFuncSetAttribute");
+    if (st == SDB_OK) done[dev][slot] = bytes;
+    return st;
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 get_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+int encode_tensor_map(CUtensorMap* map, CUtensorMapDataType dtype, cuuint32_t rank, void* base,
+                      const cuuint64_t* dims, const cuuint64_t* strides_bytes, const cuuint32_t* box,
+                      CUtensorMapSwizzle swizzle) {
+    auto enc = get_encoder();
+    if (!enc) {
+        set_last_error("cuTensorMapEncodeTiled is not available from the driver");
+        return SDB_ERR_CUDA;
+    }
+    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    CUresult r = enc(map, dtype, rank, base, dims, strides_bytes, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_last_error("cuTensorMapEncodeTiled failed with CUresult %d", (int)r);
+        return SDB_ERR_INVALID_ARG;
+    }
+    return SDB_OK;
+}
+
+}  // namespace sdb
+
+extern "C" const char* sdb_last_error(void) { return sdb::g_last_error; }
+
+extern "C" const char* sdb_build_info(void) {
+    return "specdec_b200 sm_100a: paged_attention(mma16816+TMA, simt-f32), "
+           "paged_attention_readonly, verify_batch(philox4x32-10), w8a16_linear, quantize_weight";
+}

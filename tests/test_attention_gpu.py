@@ -1,0 +1,323 @@
+"""Paged decode / verify attention on the GPU against the CPU oracle and reference goldens.
+
+Tolerances: bf16/fp16 rtol 2e-2 / atol 2e-3 (against the float64 oracle of the
+same bf16 inputs); fp32 rtol 1e-5 / atol 1e-5.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import attention as oatt
+from oracle.numerics import allclose_report, bf16_bits_to_f32
+
+pytestmark = pytest.mark.gpu
+
+BF16_TOL = dict(rtol=2e-2, atol=2e-3)
+FP32_TOL = dict(rtol=1e-5, atol=1e-5)
+
+
+def _oracle(case):
+    return oatt.paged_attention(case.q.float().cpu().numpy(), case.k_cache.float().cpu().numpy(),
+                                case.v_cache.float().cpu().numpy(), case.block_tables.cpu().numpy(),
+                                case.cache_seqlens.cpu().numpy(), case.scale, n_q=case.n_q,
+                                compute_dtype=np.float64)
+
+
+def _check(got, want, tol):
+    ok, err, viol = allclose_report(got.float().cpu().numpy(), want, **tol)
+    assert ok, f"max abs err {err}, worst violation {viol}"
+
+
+@pytest.fixture(scope="module")
+def W(pkg):
+    from specdec_nanovllm_b200 import workloads
+    return workloads
+
+
+# ------------------------------------------------------------------ goldens
+def test_golden_decode_fp32(pkg, golden):
+    g = golden("attn_decode_fp32")
+    dev = "cuda"
+    out = pkg.paged_attention(torch.from_numpy(g["q"]).to(dev), torch.from_numpy(g["k_cache"]).to(dev),
+                              torch.from_numpy(g["v_cache"]).to(dev),
+                              torch.from_numpy(g["block_tables"]).to(dev),
+                              torch.from_numpy(g["cache_seqlens"]).to(dev), float(g["scale"]), n_q=1)
+    torch.cuda.synchronize()
+    _check(out, g["out"], FP32_TOL)
+
+
+@pytest.mark.parametrize("n_q", [1, 4])
+def test_golden_bf16(pkg, golden, n_q):
+    g = golden(f"attn_bf16_nq{n_q}")
+    dev = "cuda"
+
+    def t(bits):
+        return torch.from_numpy(bf16_bits_to_f32(bits)).to(torch.bfloat16).to(dev)
+
+    out = pkg.paged_attention(t(g["q"]), t(g["k_cache"]), t(g["v_cache"]),
+                              torch.from_numpy(g["block_tables"]).to(dev),
+                              torch.from_numpy(g["cache_seqlens"]).to(dev), float(g["scale"]), n_q=n_q)
+    torch.cuda.synchronize()
+    _check(out, g["out_f32"], BF16_TOL)
+
+
+# ------------------------------------------------------------------ configs
+def test_cfg1_decode_fp32(pkg, W):
+    case = W.cfg1_case(seed=0)
+    out = pkg.paged_attention(case.q, case.k_cache, case.v_cache, case.block_tables, case.cache_seqlens,
+                              case.scale, n_q=1)
+    torch.cuda.synchronize()
+    _check(out, _oracle(case), FP32_TOL)
+
+
+@pytest.mark.parametrize("B,ctx", [(1, 512), (8, 512), (8, 2048), (1, 4096)])
+@pytest.mark.parametrize("n_q", [7, 1])
+def test_cfg2_verify_and_decode(pkg, W, B, ctx, n_q):
+    lens = W.cfg2_lens(B, ctx, seed=B + ctx)
+    case = W.paged_case(lens, n_q, seed=ctx + n_q, max_blocks=ctx // 256, **W.QWEN3_4B)
+    out = pkg.paged_attention(case.q, case.k_cache, case.v_cache, case.block_tables, case.cache_seqlens,
+                              case.scale, n_q=n_q)
+    torch.cuda.synchronize()
+    _check(out, _oracle(case), BF16_TOL)
+
+
+@pytest.mark.parametrize("splits", [1, 2, 3, 7, 16])
+def test_any_split_count(pkg, W, splits):
+    lens = [2048, 2047, 1, 256, 1025, 7]
+    case = W.paged_case(lens, 7, seed=splits, max_blocks=8, **W.QWEN3_4B)
+    out = pkg.paged_attention(case.q, case.k_cache, case.v_cache, case.block_tables, case.cache_seqlens,
+                              case.scale, n_q=7, splits=splits)
+    torch.cuda.synchronize()
+    _check(out, _oracle(case), BF16_TOL)
+
+
+@pytest.mark.parametrize("Hq,Hkv,n_q", [(16, 8, 1), (16, 8, 7), (32, 8, 2), (8, 8, 5), (64, 8, 8),
+                                        (4, 1, 7), (32, 4, 7)])
+def test_gqa_groups_and_row_counts(pkg, W, Hq, Hkv, n_q):
+    lens = [300, 256, 9, 1000]
+    case = W.paged_case(lens, n_q, Hq=Hq, Hkv=Hkv, D=128, seed=Hq * 10 + n_q, max_blocks=4)
+    out = pkg.paged_attention(case.q, case.k_cache, case.v_cache, case.block_tables, case.cache_seqlens,
+                              case.scale, n_q=n_q)
+    torch.cuda.synchronize()
+    _check(out, _oracle(case), BF16_TOL)
+
+
+def test_fp16_and_page_512(pkg, W):
+    lens = [700, 512, 33]
+    case = W.paged_case(lens, 7, page=512, dtype=torch.float16, seed=5, max_blocks=2, **W.QWEN3_4B)
+    out = pkg.paged_attention(case.q, case.k_cache, case.v_cache, case.block_tables, case.cache_seqlens,
+                              case.scale, n_q=7)
+    torch.cuda.synchronize()
+    _check(out, _oracle(case), BF16_TOL)
+
+
+def test_edge_lengths_zero_and_shorter_than_window(pkg, W):
+    # L = 0 (graph pad row), L < n_q (rows with no visible key), L = 1, exact pages
+    lens = [0, 3, 1, 256, 512, 0, 6]
+    case = W.paged_case(lens, 7, seed=11, max_blocks=2, **W.QWEN3_4B)
+    out = pkg.paged_attention(case.q, case.k_cache, case.v_cache, case.block_tables, case.cache_seqlens,
+                              case.scale, n_q=7)
+    torch.cuda.synchronize()
+    want = _oracle(case)
+    _check(out, want, BF16_TOL)
+    o = out.float().cpu()
+    assert torch.all(o[0:7] == 0) and torch.all(o[35:42] == 0)       # L = 0 sequences
+    assert torch.all(o[7:7 + 4] == 0)                                 # L=3: rows 0..3 see nothing
+    assert torch.isfinite(o).all()
+
+
+def test_pad_rows_block_zero_ctx_zero(pkg, W):
+    """Graph padding rule (graph_pad.py:33-69): block table row of zeros, ctx 0 -> zeros, no NaN."""
+    case = W.paged_case([500, 1], 7, seed=2, max_blocks=2, **W.QWEN3_4B)
+    bt = torch.cat([case.block_tables, torch.zeros(2, 2, dtype=torch.int32, device="cuda")])
+    cl = torch.cat([case.cache_seqlens, torch.zeros(2, dtype=torch.int32, device="cuda")])
+    q = torch.cat([case.q, torch.randn(14, 32, 128, device="cuda").to(torch.bfloat16)])
+    out = pkg.paged_attention(q, case.k_cache, case.v_cache, bt, cl, case.scale, n_q=7)
+    torch.cuda.synchronize()
+    assert torch.all(out[14:] == 0)
+    _check(out[:14], _oracle(case), BF16_TOL)
+
+
+def test_head_major_layout(pkg, W):
+    case = W.paged_case([400, 77], 1, seed=8, max_blocks=2, **W.QWEN3_4B)
+    k_hm = case.k_cache.permute(0, 2, 1, 3).contiguous().permute(0, 2, 1, 3)
+    v_hm = case.v_cache.permute(0, 2, 1, 3).contiguous().permute(0, 2, 1, 3)
+    out = pkg.paged_attention(case.q, k_hm, v_hm, case.block_tables, case.cache_seqlens, case.scale)
+    torch.cuda.synchronize()
+    _check(out, _oracle(case), BF16_TOL)
+
+
+# ------------------------------------------------------------------ properties at full size
+def test_full_size_verify_rows_equal_truncated_decodes(pkg, W):
+    """B=64, ctx=4096, k=6: verify row r is bit-identical to a decode of length L-6+r,
+    and a sample of sequences matches the oracle."""
+    B, ctx, n_q = 64, 4096, 7
+    case = W.paged_case([ctx] * B, n_q, seed=1, generate_on_device=True, extra_blocks=0, **W.QWEN3_4B)
+    out = pkg.paged_attention(case.q, case.k_cache, case.v_cache, case.block_tables, case.cache_seqlens,
+                              case.scale, n_q=n_q)
+    qv = case.q.view(B, n_q, 32, 128)
+    splits = pkg.attention.default_splits(B, n_q, 32, 8, 128, 256, 16, torch.bfloat16)
+    for r in range(n_q):
+        lens_r = case.cache_seqlens - (n_q - 1) + r
+        dec = pkg.paged_attention(qv[:, r].contiguous(), case.k_cache, case.v_cache, case.block_tables,
+                                  lens_r, case.scale, n_q=1, splits=splits)
+        assert torch.equal(dec, out.view(B, n_q, 32, 128)[:, r]), f"row {r}"
+    sample = [0, 17, 63]
+    sub = W.PagedCase(q=qv[sample].reshape(-1, 32, 128), k_cache=case.k_cache, v_cache=case.v_cache,
+                      block_tables=case.block_tables[sample], cache_seqlens=case.cache_seqlens[sample],
+                      scale=case.scale, n_q=n_q)
+    _check(out.view(B, n_q, 32, 128)[sample].reshape(-1, 32, 128), _oracle(sub), BF16_TOL)
+
+
+def test_block_placement_invariance_and_determinism(pkg, W):
+    case = W.paged_case([3000, 1234, 4096, 17], 7, seed=4, max_blocks=16, **W.QWEN3_4B)
+    out1 = pkg.paged_attention(case.q, case.k_cache, case.v_cache, case.block_tables, case.cache_seqlens,
+                               case.scale, n_q=7)
+    out2 = pkg.paged_attention(case.q, case.k_cache, case.v_cache, case.block_tables, case.cache_seqlens,
+                               case.scale, n_q=7)
+    # move every block to a new physical slot (reverse the pool) -> identical bits
+    NB = case.k_cache.shape[0]
+    perm = torch.arange(NB - 1, -1, -1, device="cuda")
+    k2 = case.k_cache[perm]
+    v2 = case.v_cache[perm]
+    bt2 = torch.where(case.block_tables >= 0, NB - 1 - case.block_tables, case.block_tables)
+    out3 = pkg.paged_attention(case.q, k2, v2, bt2.to(torch.int32), case.cache_seqlens, case.scale, n_q=7)
+    torch.cuda.synchronize()
+    assert torch.equal(out1, out2)
+    assert torch.equal(out1, out3)
+
+
+def test_cuda_graph_capture_and_replay(pkg, W):
+    case = W.paged_case([1500, 800], 7, seed=6, max_blocks=8, **W.QWEN3_4B)
+    out = torch.empty_like(case.q)
+    pkg.paged_attention(case.q, case.k_cache, case.v_cache, case.block_tables, case.cache_seqlens,
+                        case.scale, n_q=7, out=out)  # sizes the workspace
+    torch.cuda.synchronize()
+    ref = out.clone()
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            pkg.paged_attention(case.q, case.k_cache, case.v_cache, case.block_tables, case.cache_seqlens,
+                                case.scale, n_q=7, out=out)
+    torch.cuda.current_stream().wait_stream(s)
+    out.zero_()
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, ref)
+    # new lengths through the same graph (device data only)
+    case.cache_seqlens.copy_(torch.tensor([700, 2048], dtype=torch.int32))
+    g.replay()
+    torch.cuda.synchronize()
+    _check(out, _oracle(case), BF16_TOL)
+    del g
+
+
+def test_invalid_block_ids_are_flagged_not_faulted(pkg, W):
+    from specdec_nanovllm_b200 import _lib
+    case = W.paged_case([600], 1, seed=3, max_blocks=3, **W.QWEN3_4B)
+    bt = case.block_tables.clone()
+    bt[0, 1] = 10_000_000            # outside the pool: the kernel clamps to block 0 and flags it
+    pkg.attention.clear_error_word()
+    pkg.paged_attention(case.q, case.k_cache, case.v_cache, bt, case.cache_seqlens, case.scale, splits=1)
+    torch.cuda.synchronize()
+    assert pkg.attention.error_word() & _lib.SDB_KERR_BLOCK_ID
+    pkg.attention.clear_error_word()
+    cl = torch.tensor([10_000], dtype=torch.int32, device="cuda")  # longer than the table holds
+    pkg.paged_attention(case.q, case.k_cache, case.v_cache, case.block_tables, cl, case.scale, splits=1)
+    torch.cuda.synchronize()
+    assert pkg.attention.error_word() & _lib.SDB_KERR_SEQLEN
+    pkg.attention.clear_error_word()
+
+
+def test_host_rejects_bad_arguments(pkg, W):
+    case = W.paged_case([100], 7, seed=3, max_blocks=1, **W.QWEN3_4B)
+    with pytest.raises(ValueError):
+        pkg.paged_attention(case.q, case.k_cache, case.v_cache, case.block_tables, case.cache_seqlens,
+                            case.scale, n_q=6)            # 7 rows for B=1 is not B*n_q
+    with pytest.raises(ValueError):
+        pkg.paged_attention(case.q.float(), case.k_cache, case.v_cache, case.block_tables,
+                            case.cache_seqlens, case.scale, n_q=7)
+
+
+def test_readonly_twin_runs(pkg, W):
+    case = W.paged_case([2048] * 4, 7, seed=9, max_blocks=8, **W.QWEN3_4B)
+    pkg.paged_attention_readonly(case.q, case.k_cache, case.v_cache, case.block_tables, case.cache_seqlens, n_q=7)
+    torch.cuda.synchronize()
+    assert pkg.attention.error_word(kind="attention_ro") == 0
+
+
+# ------------------------------------------------------------------ module mirrors
+def test_store_kvcache_and_attention_module_verify_step(pkg, W):
+    """One verify step through the Attention module: store k+1 new rows, attend with
+    cu_seqlens metadata as prepare_verify builds it (model_runner.py:522-548)."""
+    from specdec_nanovllm_b200 import context as ctx
+    torch.manual_seed(0)
+    B, n_q, Hq, Hkv, D, page = 3, 7, 32, 8, 128, 256
+    lens_before = [300, 256 - 7, 1000]        # confirmed tokens already in cache
+    lens = [L + n_q for L in lens_before]
+    case = W.paged_case(lens, n_q, seed=21, max_blocks=5, **W.QWEN3_4B)
+    k_new = torch.randn(B * n_q, Hkv, D, device="cuda").to(torch.bfloat16)
+    v_new = torch.randn(B * n_q, Hkv, D, device="cuda").to(torch.bfloat16)
+    slots = []
+    bt = case.block_tables.cpu()
+    for b in range(B):
+        for pos in range(lens_before[b], lens[b]):
+            slots.append(int(bt[b, pos // page]) * page + pos % page)
+    slots[3] = -1                              # a skipped row keeps the old cache content
+    slot_mapping = torch.tensor(slots, dtype=torch.int32, device="cuda")
+    kc = case.k_cache.clone()
+    vc = case.v_cache.clone()
+    attn = pkg.Attention(Hq, D, case.scale, Hkv)
+    attn.k_cache, attn.v_cache = kc, vc
+    cu_q = torch.arange(0, (B + 1) * n_q, n_q, dtype=torch.int32, device="cuda")
+    cu_k = torch.tensor([0] + list(np.cumsum(lens)), dtype=torch.int32, device="cuda")
+    ctx.set_context(True, cu_q, cu_k, n_q, max(lens), slot_mapping, None, case.block_tables,
+                    is_spec_verify=True)
+    try:
+        out = attn(case.q, k_new, v_new)
+    finally:
+        ctx.reset_context()
+    torch.cuda.synchronize()
+    # expected cache: the stored rows land at their slots (except the skipped one)
+    kexp = case.k_cache.clone().view(-1, Hkv, D)
+    vexp = case.v_cache.clone().view(-1, Hkv, D)
+    for i, s in enumerate(slots):
+        if s >= 0:
+            kexp[s] = k_new[i]
+            vexp[s] = v_new[i]
+    assert torch.equal(kc.view(-1, Hkv, D), kexp) and torch.equal(vc.view(-1, Hkv, D), vexp)
+    want = oatt.paged_attention(case.q.float().cpu().numpy(), kexp.view_as(kc).float().cpu().numpy(),
+                                vexp.view_as(vc).float().cpu().numpy(), case.block_tables.cpu().numpy(),
+                                np.array(lens, dtype=np.int32), case.scale, n_q=n_q, compute_dtype=np.float64)
+    _check(out, want, BF16_TOL)
+
+
+def test_attention_module_decode_and_reference_mirrors(pkg, W):
+    from specdec_nanovllm_b200 import context as ctx
+    case = W.paged_case([513, 64], 1, seed=31, max_blocks=3, **W.QWEN3_06B)
+    want = _oracle(case)
+    attn = pkg.Attention(16, 128, case.scale, 8)
+    attn.k_cache, attn.v_cache = case.k_cache, case.v_cache
+    ctx.set_context(False, context_lens=case.cache_seqlens, block_tables=case.block_tables)
+    try:
+        o = attn(case.q, torch.empty(0), torch.empty(0))
+        ctx.set_context(False, context_lens=case.cache_seqlens[:1], block_tables=case.block_tables[:1])
+        o1 = attn(case.q[:1].reshape(16, 128), torch.empty(0), torch.empty(0))  # batch-1 (Hq, D) form
+    finally:
+        ctx.reset_context()
+    torch.cuda.synchronize()
+    assert o.shape == (2, 1, 16, 128)
+    _check(o.view(2, 16, 128), want, BF16_TOL)
+    o_ref_api = pkg.paged_decode_attention(case.q, case.k_cache, case.v_cache, case.block_tables,
+                                           case.cache_seqlens, case.scale)
+    o_cuda_api = pkg.paged_decode_attention_cuda(case.q, case.k_cache, case.v_cache, case.block_tables,
+                                                 case.cache_seqlens, case.scale, splits=4)
+    torch.cuda.synchronize()
+    _check(o_ref_api, want, BF16_TOL)
+    _check(o_cuda_api, want, BF16_TOL)
+    assert o1.shape == (1, 1, 16, 128)
+    _check(o1.view(1, 16, 128), want[:1], BF16_TOL)

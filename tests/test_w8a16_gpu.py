@@ -1,0 +1,121 @@
+"""W8A16 linear and quantize_weight on the GPU.
+
+quantize_weight: bit-exact against the reference (golden q and bf16 scales).
+int8_linear: rtol 2e-2 / atol 2e-3 against the float32 product x.float() @ dequant(q, s).T
+(the reference's own check, scripts/bench_int8_gemm.py:139-142), computed in float64.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import quant as oq
+from oracle.numerics import allclose_report, bf16_bits_to_f32
+
+pytestmark = pytest.mark.gpu
+
+TOL = dict(rtol=2e-2, atol=2e-3)
+
+
+def _ref(x, q, s, bias=None, granularity="per_channel", group_size=128):
+    w = (q.double() * s.double().unsqueeze(1) if granularity == "per_channel" else
+         (q.double().view(q.shape[0], -1, group_size) * s.double().unsqueeze(-1)).view(q.shape))
+    y = x.double() @ w.T
+    if bias is not None:
+        y = y + bias.double()
+    return y
+
+
+def _check(got, want):
+    ok, err, viol = allclose_report(got.float().cpu().numpy(), want.cpu().numpy(), **TOL)
+    assert ok, f"max abs err {err}, worst violation {viol}"
+
+
+@pytest.mark.parametrize("gran,gs", [("per_channel", 128), ("per_group", 64)])
+def test_quantize_weight_bit_exact_vs_reference(pkg, golden, gran, gs):
+    g = golden("quant")
+    w = torch.from_numpy(g["w"]).cuda()
+    q, s = pkg.quantize_weight(w, gran, gs)
+    torch.cuda.synchronize()
+    assert np.array_equal(q.cpu().numpy(), g[f"{gran}_q"])
+    assert np.array_equal(s.cpu().view(torch.int16).numpy().view(np.uint16), g[f"{gran}_scale"])
+
+
+@pytest.mark.parametrize("gran,gs", [("per_channel", 128), ("per_group", 64)])
+def test_int8_linear_golden(pkg, golden, gran, gs):
+    g = golden("quant")
+    x = torch.from_numpy(bf16_bits_to_f32(g["x"])).to(torch.bfloat16).cuda()
+    q = torch.from_numpy(g[f"{gran}_q"]).cuda()
+    s = torch.from_numpy(bf16_bits_to_f32(g[f"{gran}_scale"])).to(torch.bfloat16).cuda()
+    y = pkg.int8_linear(x, q, s, granularity=gran, group_size=gs)
+    torch.cuda.synchronize()
+    ok, err, _ = allclose_report(y.float().cpu().numpy(), g[f"{gran}_y"], **TOL)
+    assert ok, err
+
+
+@pytest.mark.parametrize("name", ["qkv", "o", "gate_up", "down"])
+@pytest.mark.parametrize("M", [1, 7, 64, 448])
+def test_cfg3_shapes(pkg, name, M):
+    from specdec_nanovllm_b200.workloads import W8A16_SHAPES, cfg3_inputs
+    K, N = W8A16_SHAPES[name]
+    x, q, s = cfg3_inputs(M, K, N, seed=M)
+    y = pkg.int8_linear(x, q, s)
+    torch.cuda.synchronize()
+    assert y.dtype == torch.float16 and y.shape == (M, N)
+    _check(y, _ref(x, q, s))
+
+
+@pytest.mark.parametrize("M", [3, 40])
+def test_bf16_bias_and_odd_shapes(pkg, M):
+    g = torch.Generator(device="cuda").manual_seed(5)
+    N, K = 200, 320                              # N not a multiple of the 64-feature tile
+    q = torch.randint(-127, 128, (N, K), generator=g, device="cuda", dtype=torch.int32).to(torch.int8)
+    s = (torch.rand(N, generator=g, device="cuda") * 0.01).to(torch.bfloat16)
+    x = torch.randn(M, K, generator=g, device="cuda").to(torch.bfloat16)
+    bias = torch.randn(N, generator=g, device="cuda").to(torch.bfloat16)
+    y = pkg.int8_linear(x.view(M, K), q, s, bias)
+    torch.cuda.synchronize()
+    _check(y, _ref(x, q, s, bias))
+
+
+@pytest.mark.parametrize("M", [1, 64])
+def test_per_group_fp32_scales(pkg, M):
+    g = torch.Generator(device="cuda").manual_seed(9)
+    N, K, G = 512, 1024, 128
+    q = torch.randint(-127, 128, (N, K), generator=g, device="cuda", dtype=torch.int32).to(torch.int8)
+    s = torch.rand(N, K // G, generator=g, device="cuda") * 0.01
+    x = torch.randn(M, K, generator=g, device="cuda").to(torch.float16)
+    y = pkg.int8_linear(x, q, s, granularity="per_group", group_size=G)
+    torch.cuda.synchronize()
+    _check(y, _ref(x, q, s, granularity="per_group", group_size=G))
+
+
+def test_quantize_then_linear_matches_dequantized_product(pkg):
+    g = torch.Generator(device="cuda").manual_seed(1)
+    w = torch.randn(6144, 2560, generator=g, device="cuda") * 0.02
+    q, s = pkg.quantize_weight(w)
+    x = torch.randn(7, 2560, generator=g, device="cuda").to(torch.bfloat16)
+    y = pkg.int8_linear(x, q, s)
+    torch.cuda.synchronize()
+    _check(y, x.double() @ pkg.dequantize_weight(q, s).double().T)
+    qo, so = oq.quantize_weight(w.cpu().numpy())
+    assert np.array_equal(q.cpu().numpy(), qo)
+
+
+def test_deterministic_and_graph_capturable(pkg):
+    from specdec_nanovllm_b200.workloads import cfg3_inputs
+    x, q, s = cfg3_inputs(1, 9728, 2560, seed=2)
+    y1 = pkg.int8_linear(x, q, s)
+    y = torch.empty_like(y1)
+    g = torch.cuda.CUDAGraph()
+    st = torch.cuda.Stream()
+    st.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(st):
+        with torch.cuda.graph(g, stream=st):
+            pkg.int8_linear(x, q, s, out=y)
+    torch.cuda.current_stream().wait_stream(st)
+    g.replay()
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(y, y1)
+    del g
