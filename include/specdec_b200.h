@@ -71,7 +71,7 @@ const char* sdb_build_info(void);
  *
  * dtype: SDB_BF16 / SDB_F16 (tensor-core path: D = 128, page % 64 == 0,
  *        n_q*Hq/Hkv <= 64) or SDB_F32 (CUDA-core path, fp32 accumulate, any
- *        page, D in {64, 128, 256}, n_q*Hq/Hkv <= 32).
+ *        page, D in {32, 64, 128, 256}, n_q*Hq/Hkv <= 64).  B * Hkv <= 65536.
  * splits: KV splits per (sequence, kv head); 0 picks a default from the static
  *         shape (max_blocks * page), never from device data.
  * workspace: sdb_paged_attention_workspace_size() bytes, 256-byte aligned,

@@ -15,8 +15,8 @@
 //     guarded by full/empty mbarriers.  A tile never crosses a page because
 //     page % 64 == 0, so one block-table lookup feeds four TMA boxes.
 //   * the GQA group of query heads times the n_q query rows of the sequence form
-//     the M dimension: rows rho = r*G + g, padded to MT m16 tiles.  MT x KG
-//     consumer warps: warp (mt, kg) owns m-tile mt and every KG-th tile.
+//     the M dimension: rows rho = r*G + g, padded to MT m16 tiles; consumer warp
+//     mt owns m-tile mt and consumes every K/V tile of the split.
 //     S = Q K^T and O += P V run on mma.m16n8k16 with fp32 accumulators; P is
 //     re-packed from the S accumulators in registers; the row max / row sum use
 //     quad shuffles; exp is MUFU ex2 on log2-scaled logits.
@@ -28,6 +28,7 @@
 // bottom of this file.
 #include <cfloat>
 #include <cstdio>
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -62,13 +63,18 @@ struct WsLayout {
     size_t err, counters, part_ml, part_o, total;
 };
 
+// The split-merge counters live at a fixed offset with a fixed capacity, so one
+// workspace can serve calls of any shape in any order: a counter slot is never
+// aliased by another call's partials, and every kernel leaves its counters at 0.
+constexpr int kCounterCap = 65536;  // (sequence, kv head) pairs
+
 static WsLayout ws_layout(int B, int R, int Hkv, int splits) {
     WsLayout w;
     size_t off = 0;
     w.err = off;
     off += 256;
     w.counters = off;
-    off = align_up(off + sizeof(int) * (size_t)B * Hkv, 256);
+    off = align_up(off + sizeof(int) * (size_t)kCounterCap, 256);
     const size_t slots = (size_t)B * Hkv * (splits > 1 ? splits : 0);
     w.part_ml = off;
     off = align_up(off + sizeof(float) * slots * R * 2, 256);
@@ -137,12 +143,12 @@ SDB_DEV uint32_t tile_addr(uint32_t base, int row, int c) {
     return base + (c >> 3) * HALF_BYTES + row * 128 + (((c & 7) ^ (row & 7)) << 4);
 }
 
-template <typename T, int MT, int KG, int NS>
-__global__ void __launch_bounds__((MT * KG + 1) * 32)
+template <typename T, int MT, int NS>
+__global__ void __launch_bounds__((MT + 1) * 32)
     pa_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
                   const Params p) {
     using H = Half16<T>;
-    constexpr int NC = MT * KG;
+    constexpr int NC = MT;  // consumer warps; every one of them consumes every tile
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
@@ -176,8 +182,9 @@ __global__ void __launch_bounds__((MT * KG + 1) * 32)
     }
 
     // ------------------------------------------------------------ consumers
-    const int mt = warp % MT;
-    const int kg = warp / MT;
+    // Every consumer warp takes every tile, so each stage's fills are awaited in
+    // order and a parity wait can never be satisfied by an older phase.
+    const int mt = warp;
     const int R = p.R;
     const int rho0 = mt * 16 + (lane >> 2);
     const int rho1 = rho0 + 8;
@@ -219,7 +226,7 @@ __global__ void __launch_bounds__((MT * KG + 1) * 32)
     for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
 
     const float sl2 = p.scale_log2;
-    for (int t = kg; t < ntiles; t += KG) {
+    for (int t = 0; t < ntiles; ++t) {
         const int s = t % NS;
         if (!mbar_wait(full0 + 8 * s, (t / NS) & 1)) {
             if (lane == 0) atomicOr(p.err, SDB_KERR_TIMEOUT);
@@ -336,54 +343,7 @@ __global__ void __launch_bounds__((MT * KG + 1) * 32)
     l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
     l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
 
-    // ------------------------------------------ merge key groups (stage ring reused)
-    if (KG > 1) {
-        named_barrier_sync(1, NC * 32);
-        float* scr = reinterpret_cast<float*>(smem);  // [(KG-1)][MT][16][D+2]
-        constexpr int ROWF = D + 2;
-        if (kg > 0) {
-            float* base = scr + ((kg - 1) * MT + mt) * 16 * ROWF;
-            const int ra = lane >> 2, rb = ra + 8;
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                *reinterpret_cast<float2*>(base + ra * ROWF + i * 8 + cq) = make_float2(o[i][0], o[i][1]);
-                *reinterpret_cast<float2*>(base + rb * ROWF + i * 8 + cq) = make_float2(o[i][2], o[i][3]);
-            }
-            if ((lane & 3) == 0) {
-                base[ra * ROWF + D] = m0;
-                base[ra * ROWF + D + 1] = l0;
-                base[rb * ROWF + D] = m1;
-                base[rb * ROWF + D + 1] = l1;
-            }
-        }
-        named_barrier_sync(1, NC * 32);
-        if (kg > 0) return;
-        const int ra = lane >> 2, rb = ra + 8;
-        for (int g2 = 1; g2 < KG; ++g2) {
-            const float* base = scr + ((g2 - 1) * MT + mt) * 16 * ROWF;
-            const float om0 = base[ra * ROWF + D], ol0 = base[ra * ROWF + D + 1];
-            const float om1 = base[rb * ROWF + D], ol1 = base[rb * ROWF + D + 1];
-            const float M0 = fmaxf(m0, om0), M1 = fmaxf(m1, om1);
-            const float B0 = M0 == NEG_INF ? 0.f : M0, B1 = M1 == NEG_INF ? 0.f : M1;
-            const float w0 = ex2(m0 - B0), v0 = ex2(om0 - B0);
-            const float w1 = ex2(m1 - B1), v1 = ex2(om1 - B1);
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-                const float2 x = *reinterpret_cast<const float2*>(base + ra * ROWF + i * 8 + cq);
-                const float2 y = *reinterpret_cast<const float2*>(base + rb * ROWF + i * 8 + cq);
-                o[i][0] = o[i][0] * w0 + x.x * v0;
-                o[i][1] = o[i][1] * w0 + x.y * v0;
-                o[i][2] = o[i][2] * w1 + y.x * v1;
-                o[i][3] = o[i][3] * w1 + y.y * v1;
-            }
-            l0 = l0 * w0 + ol0 * v0;
-            l1 = l1 * w1 + ol1 * v1;
-            m0 = M0;
-            m1 = M1;
-        }
-    }
-
-    // ------------------------------------------ epilogue (warps mt = 0..MT-1)
+    // ------------------------------------------ epilogue
     T* obase = reinterpret_cast<T*>(p.out);
     if (p.splits == 1) {
         const float inv0 = l0 > 0.f ? 1.f / l0 : 0.f;
@@ -649,14 +609,26 @@ __global__ void store_kvcache_kernel(const uint8_t* __restrict__ key, int64_t ks
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
-constexpr int NS_MMA = 3;
-constexpr int NS_RO = 4;
-// splits x R (<= 64) fp32 merge coefficients must fit the NS_MMA-stage ring (96 KB)
+// Stage counts per m-tile count: one consumer warp (decode) runs 3 CTAs per SM on
+// a 2-stage ring; 2 or 4 consumer warps (verify) run 2 CTAs per SM on 3 stages.
+template <int MT>
+struct Stages {
+    static constexpr int NS = MT == 1 ? 2 : 3;
+};
+constexpr int kMaxStages = 3;
+constexpr int kSmemPerSM = 233472;  // 228 KB on sm_100
+// splits x R (<= 64) fp32 merge coefficients must fit the smallest stage ring (64 KB)
 constexpr int kMaxSplits = 256;
-static_assert(kMaxSplits * 64 * 4 <= NS_MMA * STAGE_BYTES, "merge scratch exceeds the stage ring");
+static_assert(kMaxSplits * 64 * 4 <= 2 * STAGE_BYTES, "merge scratch exceeds the stage ring");
 
-static int smem_bytes_mma() { return NS_MMA * STAGE_BYTES + 1024 + 2 * NS_MMA * 8 + 16; }
-static int smem_bytes_ro() { return NS_RO * STAGE_BYTES + 1024 + 2 * NS_RO * 8 + 16; }
+static int smem_bytes_ring(int ns) { return ns * STAGE_BYTES + 1024 + 2 * ns * 8 + 16; }
+static int smem_bytes_ro() { return 4 * STAGE_BYTES + 1024 + 2 * 4 * 8 + 16; }
+static int mt_for_rows(int R) { return R <= 16 ? 1 : (R <= 32 ? 2 : 4); }
+static int ctas_per_sm(int R) {
+    const int ns = mt_for_rows(R) == 1 ? Stages<1>::NS : Stages<2>::NS;
+    const int c = kSmemPerSM / (smem_bytes_ring(ns) + 1024);
+    return c < 1 ? 1 : c;
+}
 
 static bool mma_path(int dtype, int D_, int page, int R) {
     return (dtype == SDB_BF16 || dtype == SDB_F16) && D_ == D && page % BN == 0 && R <= 64;
@@ -667,7 +639,7 @@ static int pick_splits(int B, int R, int Hkv, int page, int max_blocks, int sms)
     const long long max_ctx = (long long)max_blocks * page;
     const long long tiles = (max_ctx + BN - 1) / BN;
     const long long pairs = (long long)B * Hkv;
-    const long long slots = (long long)sms * 2;  // two CTAs per SM at NS_MMA stages
+    const long long slots = (long long)sms * ctas_per_sm(R);
     int best = 1;
     double best_cost = 1e300;
     for (int s = 1; s <= 64; ++s) {
@@ -737,9 +709,10 @@ int validate(const void* q, const void* k_cache, const void* v_cache, const int3
                        Hkv, D_, page, max_blocks, num_blocks);
         return SDB_ERR_INVALID_ARG;
     }
-    if (q_srow < (int64_t)Hq * 0 || q_shead < D_ || sh < D_ || sp < (int64_t)Hkv * sh || sb < (int64_t)page * sp ||
-        bt_stride < max_blocks) {
-        set_last_error("unsupported strides (need contiguous head_dim and non-overlapping rows)");
+    // head_dim is the contiguous axis of q and of the caches; the other cache axes may
+    // come in any order (the reference also supports a head-major layout).
+    if (q_srow <= 0 || q_shead < D_ || sh <= 0 || sp <= 0 || sb <= 0 || bt_stride < max_blocks) {
+        set_last_error("unsupported strides (need a contiguous head_dim and positive strides)");
         return SDB_ERR_INVALID_ARG;
     }
     if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0) {
@@ -749,22 +722,25 @@ int validate(const void* q, const void* k_cache, const void* v_cache, const int3
     return SDB_OK;
 }
 
-template <typename T, int MT, int KG>
+template <typename T, int MT>
 int launch_mma(const CUtensorMap& km, const CUtensorMap& vm, const Params& p, dim3 grid, cudaStream_t st, int slot) {
-    auto kern = pa_mma_kernel<T, MT, KG, NS_MMA>;
-    const int smem = smem_bytes_mma();
+    constexpr int NS = Stages<MT>::NS;
+    auto kern = pa_mma_kernel<T, MT, NS>;
+    const int smem = smem_bytes_ring(NS);
     int rc = ensure_smem_attr(reinterpret_cast<const void*>(kern), smem, slot);
     if (rc) return rc;
-    kern<<<grid, (MT * KG + 1) * 32, smem, st>>>(km, vm, p);
+    kern<<<grid, (MT + 1) * 32, smem, st>>>(km, vm, p);
     return cuda_status(cudaGetLastError(), "pa_mma_kernel launch");
 }
 
 template <typename T>
 int dispatch_mma(const CUtensorMap& km, const CUtensorMap& vm, const Params& p, dim3 grid, cudaStream_t st) {
     const int base = std::is_same<T, __half>::value ? 10 : 0;
-    if (p.R <= 16) return launch_mma<T, 1, 2>(km, vm, p, grid, st, base + 0);
-    if (p.R <= 32) return launch_mma<T, 2, 2>(km, vm, p, grid, st, base + 1);
-    return launch_mma<T, 4, 1>(km, vm, p, grid, st, base + 2);
+    switch (mt_for_rows(p.R)) {
+        case 1: return launch_mma<T, 1>(km, vm, p, grid, st, base + 0);
+        case 2: return launch_mma<T, 2>(km, vm, p, grid, st, base + 1);
+        default: return launch_mma<T, 4>(km, vm, p, grid, st, base + 2);
+    }
 }
 
 int make_maps(CUtensorMap* km, CUtensorMap* vm, const void* k_cache, const void* v_cache, int dtype, int Hkv,
@@ -835,6 +811,11 @@ extern "C" int sdb_paged_attention(const void* q, int64_t q_srow, int64_t q_shea
         if (chunk < BN) chunk = BN;
         splits = (int)((max_ctx + chunk - 1) / chunk);  // drop splits that can never hold a key
         if (splits < 1) splits = 1;
+        if ((long long)B * Hkv > kCounterCap) {
+            set_last_error("B * Hkv = %lld exceeds the supported %d (sequence, kv head) pairs", (long long)B * Hkv,
+                           kCounterCap);
+            return SDB_ERR_UNSUPPORTED;
+        }
         WsLayout w = ws_layout(B, R, Hkv, splits);
         if (workspace_bytes < w.total) {
             set_last_error("workspace too small: need %zu bytes, got %zu", w.total, workspace_bytes);
@@ -856,7 +837,7 @@ extern "C" int sdb_paged_attention(const void* q, int64_t q_srow, int64_t q_shea
     }
 
     // CUDA-core path (fp32 KV, or shapes outside the tensor-core kernel)
-    if (!(D_ == 64 || D_ == 128 || D_ == 256) || R > 64) {
+    if (!(D_ == 32 || D_ == 64 || D_ == 128 || D_ == 256) || R > 64) {
         set_last_error("unsupported shape for the CUDA-core path: D=%d rows=%d", D_, R);
         return SDB_ERR_UNSUPPORTED;
     }
@@ -872,15 +853,18 @@ extern "C" int sdb_paged_attention(const void* q, int64_t q_srow, int64_t q_shea
     pa_simt_kernel<T, DPL, 8><<<grid, 128, 0, st>>>(p, reinterpret_cast<const T*>(k_cache),                 \
                                                     reinterpret_cast<const T*>(v_cache), sb, sp, sh)
     if (dtype == SDB_F32) {
-        if (D_ == 64) SDB_SIMT(float, 2);
+        if (D_ == 32) SDB_SIMT(float, 1);
+        else if (D_ == 64) SDB_SIMT(float, 2);
         else if (D_ == 128) SDB_SIMT(float, 4);
         else SDB_SIMT(float, 8);
     } else if (dtype == SDB_BF16) {
-        if (D_ == 64) SDB_SIMT(__nv_bfloat16, 2);
+        if (D_ == 32) SDB_SIMT(__nv_bfloat16, 1);
+        else if (D_ == 64) SDB_SIMT(__nv_bfloat16, 2);
         else if (D_ == 128) SDB_SIMT(__nv_bfloat16, 4);
         else SDB_SIMT(__nv_bfloat16, 8);
     } else {
-        if (D_ == 64) SDB_SIMT(__half, 2);
+        if (D_ == 32) SDB_SIMT(__half, 1);
+        else if (D_ == 64) SDB_SIMT(__half, 2);
         else if (D_ == 128) SDB_SIMT(__half, 4);
         else SDB_SIMT(__half, 8);
     }
@@ -934,7 +918,7 @@ extern "C" int sdb_paged_attention_readonly(const void* q, int64_t q_srow, int64
     CUtensorMap km, vm;
     rc = make_maps(&km, &vm, k_cache, v_cache, dtype, Hkv, page, num_blocks, sb, sp, sh);
     if (rc) return rc;
-    auto kern = pa_readonly_kernel<NS_RO>;
+    auto kern = pa_readonly_kernel<4>;
     rc = ensure_smem_attr(reinterpret_cast<const void*>(kern), smem_bytes_ro(), 30);
     if (rc) return rc;
     kern<<<dim3(splits, Hkv, B), 64, smem_bytes_ro(), reinterpret_cast<cudaStream_t>(stream)>>>(km, vm, p);

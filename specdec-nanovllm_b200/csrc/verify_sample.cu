@@ -404,6 +404,8 @@ struct WsLayout {
     size_t err, counters, dec, stats, rsum, amax, total;
 };
 
+constexpr int kCounterCap = 1 << 19;  // sequences per call
+
 static WsLayout ws_layout(int B, int k, int Tr, int V) {
     const int C1 = (V + CHUNK1 - 1) / CHUNK1;
     const int C2 = (V + CHUNK2 - 1) / CHUNK2;
@@ -411,8 +413,8 @@ static WsLayout ws_layout(int B, int k, int Tr, int V) {
     size_t off = 0;
     w.err = off;
     off += 256;
-    w.counters = off;
-    off = align_up(off + sizeof(int) * B, 256);
+    w.counters = off;  // fixed offset and capacity: never aliased by another call's data
+    off = align_up(off + sizeof(int) * (size_t)kCounterCap, 256);
     w.dec = off;
     off = align_up(off + sizeof(Decision) * B, 256);
     w.stats = off;
@@ -453,9 +455,9 @@ extern "C" int sdb_verify_batch(const float* draft, const float* target, const i
         set_last_error("null pointer argument");
         return SDB_ERR_INVALID_ARG;
     }
-    if (B <= 0 || k <= 0 || k > 32 || V <= 0 || !(Tr == k || Tr == k + 1)) {
-        set_last_error("bad sizes B=%d k=%d target_rows=%d V=%d (need 1<=k<=32, target_rows in {k, k+1})", B, k, Tr,
-                       V);
+    if (B <= 0 || B > vs::kCounterCap || k <= 0 || k > 32 || V <= 0 || !(Tr == k || Tr == k + 1)) {
+        set_last_error("bad sizes B=%d k=%d target_rows=%d V=%d (need B <= %d, 1<=k<=32, target_rows in {k, k+1})",
+                       B, k, Tr, V, vs::kCounterCap);
         return SDB_ERR_INVALID_ARG;
     }
     if ((reinterpret_cast<uintptr_t>(workspace) & 255) ||

@@ -276,11 +276,16 @@ struct WsLayout {
     size_t counters, part, total;
 };
 
+// Split-K counters at a fixed offset with a fixed capacity: one workspace serves
+// calls of any shape in any order (counters are never aliased by partials and
+// every call leaves them at 0).
+constexpr int kCounterCap = 65536;  // output tiles
+
 static WsLayout ws_layout(int M, int N, int K) {
     Plan pl = plan(M, N, K);
     WsLayout w;
     w.counters = 0;
-    size_t off = align_up(sizeof(int) * (size_t)pl.mt * pl.nt_n, 256);
+    size_t off = align_up(sizeof(int) * (size_t)kCounterCap, 256);
     w.part = off;
     if (pl.SK > 1) off = align_up(off + sizeof(float) * (size_t)pl.SK * M * N, 256);
     w.total = off;
@@ -349,6 +354,10 @@ extern "C" int sdb_w8a16_linear(const void* x, int64_t x_srow, const int8_t* qwe
         return SDB_ERR_WORKSPACE;
     }
     w8::Plan pl = w8::plan(M, N, K);
+    if ((long long)pl.mt * pl.nt_n > w8::kCounterCap) {
+        set_last_error("M x N too large: %d output tiles (max %d)", pl.mt * pl.nt_n, w8::kCounterCap);
+        return SDB_ERR_UNSUPPORTED;
+    }
     w8::Params p{};
     p.x = x;
     p.x_srow = x_srow;
