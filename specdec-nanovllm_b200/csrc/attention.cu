@@ -15,8 +15,14 @@
 //     guarded by full/empty mbarriers.  A tile never crosses a page because
 //     page % 64 == 0, so one block-table lookup feeds four TMA boxes.
 //   * the GQA group of query heads times the n_q query rows of the sequence form
-//     the M dimension: rows rho = r*G + g, padded to MT m16 tiles; consumer warp
-//     mt owns m-tile mt and consumes every K/V tile of the split.
+//     the M dimension: rows rho = r*G + g, padded to MT m16 tiles.  MT x KG = 4
+//     consumer warps: warp (mt, kg) owns m-tile mt and a 64/KG-key slice of every
+//     tile; every consumer waits for and releases every stage, and the KG
+//     partial softmax states are merged through shared memory at the end.
+//   * P is split into a 16-bit head and a 16-bit residual (P = P_hi + P_lo) and
+//     both multiply V, so the probabilities keep ~16 significant bits: the
+//     rows of a short verify window (a few visible keys) would otherwise carry
+//     the 8-bit rounding of P straight into the output.
 //     S = Q K^T and O += P V run on mma.m16n8k16 with fp32 accumulators; P is
 //     re-packed from the S accumulators in registers; the row max / row sum use
 //     quad shuffles; exp is MUFU ex2 on log2-scaled logits.
@@ -143,12 +149,19 @@ SDB_DEV uint32_t tile_addr(uint32_t base, int row, int c) {
     return base + (c >> 3) * HALF_BYTES + row * 128 + (((c & 7) ^ (row & 7)) << 4);
 }
 
-template <typename T, int MT, int NS>
-__global__ void __launch_bounds__((MT + 1) * 32)
+template <typename T, int MT, int KG, int NS>
+__global__ void __launch_bounds__((MT * KG + 1) * 32)
     pa_mma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
                   const Params p) {
     using H = Half16<T>;
-    constexpr int NC = MT;  // consumer warps; every one of them consumes every tile
+    // Consumer warp (mt, kg) = warp mt + MT*kg owns m-tile mt and keys
+    // [kg*SK, (kg+1)*SK) of every tile.  Every consumer warp waits for and
+    // releases every stage, so each stage's phases are awaited in order.
+    constexpr int NC = MT * KG;
+    constexpr int SK = BN / KG;       // keys per warp per tile: 64, 32 or 16
+    constexpr int NKT = SK / 8;       // n8 tiles of keys in S
+    constexpr int NKK = SK / 16;      // k16 steps of keys in P.V
+    static_assert(SK % 16 == 0, "key slice must hold whole k16 steps");
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
@@ -170,25 +183,25 @@ __global__ void __launch_bounds__((MT + 1) * 32)
     if (threadIdx.x == 0) {
         for (int s = 0; s < NS; ++s) {
             mbar_init(full0 + 8 * s, 1);
-            mbar_init(empty0 + 8 * s, MT);
+            mbar_init(empty0 + 8 * s, NC);
         }
         fence_mbarrier_init();
     }
     __syncthreads();
 
     if (warp == NC) {
-        if (lane == 0 && ntiles > 0) produce<NS, MT>(p, &kmap, &vmap, stage0, full0, empty0, b, kvh, k0, ntiles);
+        if (lane == 0 && ntiles > 0) produce<NS, NC>(p, &kmap, &vmap, stage0, full0, empty0, b, kvh, k0, ntiles);
         return;
     }
 
     // ------------------------------------------------------------ consumers
-    // Every consumer warp takes every tile, so each stage's fills are awaited in
-    // order and a parity wait can never be satisfied by an older phase.
-    const int mt = warp;
+    const int mt = warp % MT;
+    const int kg = warp / MT;
     const int R = p.R;
     const int rho0 = mt * 16 + (lane >> 2);
     const int rho1 = rho0 + 8;
     const int cq = 2 * (lane & 3);
+    const int kbase = kg * SK;  // first key of this warp's slice inside a tile
 
     // Q fragments (A operand) straight from global: rows rho0 / rho1.
     uint32_t qa[8][4];
@@ -234,17 +247,17 @@ __global__ void __launch_bounds__((MT + 1) * 32)
         }
         const uint32_t kb = stage0 + s * STAGE_BYTES;
         const uint32_t vb = kb + TILE_BYTES;
-        const int j0 = k0 + t * BN;
+        const int j0 = k0 + t * BN + kbase;  // first key of this warp's slice
 
-        // ---- S = Q K^T (16 x 64 per warp)
-        float sc[8][4];
+        // ---- S = Q K^T over the slice (16 x SK per warp)
+        float sc[NKT][4];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) sc[i][0] = sc[i][1] = sc[i][2] = sc[i][3] = 0.f;
+        for (int i = 0; i < NKT; ++i) sc[i][0] = sc[i][1] = sc[i][2] = sc[i][3] = 0.f;
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks) {
 #pragma unroll
-            for (int np = 0; np < 4; ++np) {
-                const int key = np * 16 + (lane & 7) + ((lane >> 4) << 3);
+            for (int np = 0; np < NKT / 2; ++np) {
+                const int key = kbase + np * 16 + (lane & 7) + ((lane >> 4) << 3);
                 const int c = ks * 2 + ((lane >> 3) & 1);
                 uint32_t b0, b1, b2, b3;
                 ldsm_x4(b0, b1, b2, b3, tile_addr(kb, key, c));
@@ -254,10 +267,10 @@ __global__ void __launch_bounds__((MT + 1) * 32)
         }
 
         // ---- scale, mask, online softmax
-        const bool masked = (j0 + BN > lim0) || (j0 + BN > lim1);
+        const bool masked = (j0 + SK > lim0) || (j0 + SK > lim1);
         float mx0 = NEG_INF, mx1 = NEG_INF;
 #pragma unroll
-        for (int nt = 0; nt < 8; ++nt) {
+        for (int nt = 0; nt < NKT; ++nt) {
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
                 float x0 = sc[nt][e] * sl2;
@@ -285,7 +298,7 @@ __global__ void __launch_bounds__((MT + 1) * 32)
         m1 = mn1;
         float ls0 = 0.f, ls1 = 0.f;
 #pragma unroll
-        for (int nt = 0; nt < 8; ++nt) {
+        for (int nt = 0; nt < NKT; ++nt) {
 #pragma unroll
             for (int e = 0; e < 2; ++e) {
                 sc[nt][e] = ex2(sc[nt][e] - base0);
@@ -304,15 +317,24 @@ __global__ void __launch_bounds__((MT + 1) * 32)
             o[i][3] *= a1;
         }
 
-        // ---- O += P V
-        const bool vmask = j0 + BN > k1;
+        // ---- O += P V with P = P_hi + P_lo (both 16-bit): the second product
+        // carries the rounding residual of P, so O keeps ~16 bits of P.
+        const bool vmask = j0 + SK > k1;
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-            uint32_t pa[4];
-            pa[0] = H::pack(sc[2 * kk][0], sc[2 * kk][1]);
-            pa[1] = H::pack(sc[2 * kk][2], sc[2 * kk][3]);
-            pa[2] = H::pack(sc[2 * kk + 1][0], sc[2 * kk + 1][1]);
-            pa[3] = H::pack(sc[2 * kk + 1][2], sc[2 * kk + 1][3]);
+        for (int kk = 0; kk < NKK; ++kk) {
+            uint32_t ph[4], pl[4];
+            {
+                const float* c0 = sc[2 * kk];
+                const float* c1 = sc[2 * kk + 1];
+                ph[0] = H::pack(c0[0], c0[1]);
+                ph[1] = H::pack(c0[2], c0[3]);
+                ph[2] = H::pack(c1[0], c1[1]);
+                ph[3] = H::pack(c1[2], c1[3]);
+                pl[0] = H::pack_residual(c0[0], c0[1], ph[0]);
+                pl[1] = H::pack_residual(c0[2], c0[3], ph[1]);
+                pl[2] = H::pack_residual(c1[0], c1[1], ph[2]);
+                pl[3] = H::pack_residual(c1[2], c1[3], ph[3]);
+            }
             // keys of this lane's B-fragment halves: kb0, kb0+1 (regs 0/2), +8 (regs 1/3)
             const int kb0 = j0 + kk * 16 + cq;
             uint32_t keep_lo = 0xffffffffu, keep_hi = 0xffffffffu;
@@ -322,7 +344,7 @@ __global__ void __launch_bounds__((MT + 1) * 32)
             }
 #pragma unroll
             for (int dp = 0; dp < 8; ++dp) {
-                const int key = kk * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
+                const int key = kbase + kk * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
                 const int c = dp * 2 + (lane >> 4);
                 uint32_t r0, r1, r2, r3;
                 ldsm_x4_t(r0, r1, r2, r3, tile_addr(vb, key, c));
@@ -330,8 +352,10 @@ __global__ void __launch_bounds__((MT + 1) * 32)
                 r2 &= keep_lo;
                 r1 &= keep_hi;
                 r3 &= keep_hi;
-                H::mma(o[2 * dp], pa, r0, r1);
-                H::mma(o[2 * dp + 1], pa, r2, r3);
+                H::mma(o[2 * dp], ph, r0, r1);
+                H::mma(o[2 * dp + 1], ph, r2, r3);
+                H::mma(o[2 * dp], pl, r0, r1);
+                H::mma(o[2 * dp + 1], pl, r2, r3);
             }
         }
         __syncwarp();
@@ -342,6 +366,52 @@ __global__ void __launch_bounds__((MT + 1) * 32)
     l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
     l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
     l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+
+    // ------------------------------------------ merge the key groups (stage ring reused)
+    if (KG > 1) {
+        named_barrier_sync(1, NC * 32);  // every consumer is past its last stage read
+        float* scr = reinterpret_cast<float*>(smem);  // [(KG-1)][MT][16][D+2]
+        constexpr int ROWF = D + 2;
+        const int ra = lane >> 2, rb = ra + 8;
+        if (kg > 0) {
+            float* base = scr + ((kg - 1) * MT + mt) * 16 * ROWF;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                *reinterpret_cast<float2*>(base + ra * ROWF + i * 8 + cq) = make_float2(o[i][0], o[i][1]);
+                *reinterpret_cast<float2*>(base + rb * ROWF + i * 8 + cq) = make_float2(o[i][2], o[i][3]);
+            }
+            if ((lane & 3) == 0) {
+                base[ra * ROWF + D] = m0;
+                base[ra * ROWF + D + 1] = l0;
+                base[rb * ROWF + D] = m1;
+                base[rb * ROWF + D + 1] = l1;
+            }
+        }
+        named_barrier_sync(1, NC * 32);
+        if (kg > 0) return;
+        for (int g2 = 1; g2 < KG; ++g2) {
+            const float* base = scr + ((g2 - 1) * MT + mt) * 16 * ROWF;
+            const float om0 = base[ra * ROWF + D], ol0 = base[ra * ROWF + D + 1];
+            const float om1 = base[rb * ROWF + D], ol1 = base[rb * ROWF + D + 1];
+            const float M0 = fmaxf(m0, om0), M1 = fmaxf(m1, om1);
+            const float B0 = M0 == NEG_INF ? 0.f : M0, B1 = M1 == NEG_INF ? 0.f : M1;
+            const float w0 = ex2(m0 - B0), v0 = ex2(om0 - B0);
+            const float w1 = ex2(m1 - B1), v1 = ex2(om1 - B1);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const float2 x = *reinterpret_cast<const float2*>(base + ra * ROWF + i * 8 + cq);
+                const float2 y = *reinterpret_cast<const float2*>(base + rb * ROWF + i * 8 + cq);
+                o[i][0] = o[i][0] * w0 + x.x * v0;
+                o[i][1] = o[i][1] * w0 + x.y * v0;
+                o[i][2] = o[i][2] * w1 + y.x * v1;
+                o[i][3] = o[i][3] * w1 + y.y * v1;
+            }
+            l0 = l0 * w0 + ol0 * v0;
+            l1 = l1 * w1 + ol1 * v1;
+            m0 = M0;
+            m1 = M1;
+        }
+    }
 
     // ------------------------------------------ epilogue
     T* obase = reinterpret_cast<T*>(p.out);
@@ -609,11 +679,10 @@ __global__ void store_kvcache_kernel(const uint8_t* __restrict__ key, int64_t ks
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
-// Stage counts per m-tile count: one consumer warp (decode) runs 3 CTAs per SM on
-// a 2-stage ring; 2 or 4 consumer warps (verify) run 2 CTAs per SM on 3 stages.
+// Stage count of the K/V ring: 3 stages of 32 KB -> 2 CTAs per SM.
 template <int MT>
 struct Stages {
-    static constexpr int NS = MT == 1 ? 2 : 3;
+    static constexpr int NS = 3;
 };
 constexpr int kMaxStages = 3;
 constexpr int kSmemPerSM = 233472;  // 228 KB on sm_100
@@ -722,24 +791,26 @@ int validate(const void* q, const void* k_cache, const void* v_cache, const int3
     return SDB_OK;
 }
 
-template <typename T, int MT>
+template <typename T, int MT, int KG>
 int launch_mma(const CUtensorMap& km, const CUtensorMap& vm, const Params& p, dim3 grid, cudaStream_t st, int slot) {
     constexpr int NS = Stages<MT>::NS;
-    auto kern = pa_mma_kernel<T, MT, NS>;
+    auto kern = pa_mma_kernel<T, MT, KG, NS>;
     const int smem = smem_bytes_ring(NS);
     int rc = ensure_smem_attr(reinterpret_cast<const void*>(kern), smem, slot);
     if (rc) return rc;
-    kern<<<grid, (MT + 1) * 32, smem, st>>>(km, vm, p);
+    kern<<<grid, (MT * KG + 1) * 32, smem, st>>>(km, vm, p);
     return cuda_status(cudaGetLastError(), "pa_mma_kernel launch");
 }
 
+// Four consumer warps per CTA in every configuration: 1 m-tile x 4 key slices
+// (decode), 2 x 2 (k+1 verify rows of a GQA-4 group), 4 x 1 (up to 64 rows).
 template <typename T>
 int dispatch_mma(const CUtensorMap& km, const CUtensorMap& vm, const Params& p, dim3 grid, cudaStream_t st) {
     const int base = std::is_same<T, __half>::value ? 10 : 0;
     switch (mt_for_rows(p.R)) {
-        case 1: return launch_mma<T, 1>(km, vm, p, grid, st, base + 0);
-        case 2: return launch_mma<T, 2>(km, vm, p, grid, st, base + 1);
-        default: return launch_mma<T, 4>(km, vm, p, grid, st, base + 2);
+        case 1: return launch_mma<T, 1, 4>(km, vm, p, grid, st, base + 0);
+        case 2: return launch_mma<T, 2, 2>(km, vm, p, grid, st, base + 1);
+        default: return launch_mma<T, 4, 1>(km, vm, p, grid, st, base + 2);
     }
 }
 

@@ -134,6 +134,12 @@ struct Half16<__nv_bfloat16> {
             : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
             : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
     }
+    // (lo - hi0, hi - hi1) rounded to bf16, where hi0/hi1 are the packed head values
+    static SDB_DEV uint32_t pack_residual(float lo, float hi, uint32_t head) {
+        __nv_bfloat162 h = *reinterpret_cast<__nv_bfloat162*>(&head);
+        const float2 f = __bfloat1622float2(h);
+        return pack(lo - f.x, hi - f.y);
+    }
     static constexpr CUtensorMapDataType tmap_type = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
 };
 
@@ -149,6 +155,11 @@ struct Half16<__half> {
             "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
             : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
             : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    }
+    static SDB_DEV uint32_t pack_residual(float lo, float hi, uint32_t head) {
+        __half2 h = *reinterpret_cast<__half2*>(&head);
+        const float2 f = __half22float2(h);
+        return pack(lo - f.x, hi - f.y);
     }
     static constexpr CUtensorMapDataType tmap_type = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
 };
