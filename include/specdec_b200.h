@@ -93,6 +93,30 @@ int sdb_paged_attention(const void* q, int64_t q_stride_row, int64_t q_stride_he
                         float softmax_scale, int dtype, int splits,
                         void* workspace, size_t workspace_bytes, void* stream);
 
+/* No-allocation variant of sdb_paged_attention (no counterpart in the reference).
+ * For callers that cannot allocate device memory when they run attention -- a
+ * plugin inside another runtime's enqueue callback whose memory pool forbids raw
+ * allocations, a steady-state serving loop that cannot afford cudaMalloc's
+ * implicit device-wide synchronisation, a deployment with a fixed memory budget.
+ * Same arguments as sdb_paged_attention without the workspace: the split
+ * partials and merge counters live in a file-scope device array of
+ * SDB_NOALLOC_SCRATCH_BYTES that every GPU loading the library holds until the
+ * process exits.  Shapes needing more scratch return SDB_ERR_WORKSPACE before any
+ * launch.  The first call on a device (that device current) looks the array up
+ * and clears its counters on the given stream; make it before anything that must
+ * not see that set-up.  All calls share the array: calls that overlap on the GPU
+ * race and must be serialised by the caller.  Allocates nothing. */
+#define SDB_NOALLOC_SCRATCH_BYTES (16u << 20)
+int sdb_paged_attention_noalloc(const void* q, int64_t q_stride_row, int64_t q_stride_head,
+                                const void* k_cache, const void* v_cache,
+                                int64_t kv_stride_block, int64_t kv_stride_page, int64_t kv_stride_head,
+                                const int32_t* block_tables, int64_t bt_stride,
+                                const int32_t* cache_seqlens,
+                                void* out, int64_t o_stride_row, int64_t o_stride_head,
+                                int B, int n_q, int Hq, int Hkv, int D, int page,
+                                int max_blocks, int num_blocks,
+                                float softmax_scale, int dtype, int splits, void* stream);
+
 /* Memory-floor twin of sdb_paged_attention: the same grid, the same TMA loads
  * of every visible K/V tile, no math; writes one checksum word per CTA into the
  * workspace.  Reference counterpart: paged_decode_readonly_kernel,

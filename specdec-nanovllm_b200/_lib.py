@@ -56,6 +56,10 @@ SIGNATURES = {
         _c_p, _c_i64, _c_i64, _c_p, _c_p, _c_i64, _c_i64, _c_i64, _c_p, _c_i64, _c_p,
         _c_p, _c_i64, _c_i64, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32,
         _c_f32, _c_i32, _c_i32, _c_p, _c_sz, _c_p]),
+    "sdb_paged_attention_noalloc": (_c_i32, [
+        _c_p, _c_i64, _c_i64, _c_p, _c_p, _c_i64, _c_i64, _c_i64, _c_p, _c_i64, _c_p,
+        _c_p, _c_i64, _c_i64, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32,
+        _c_f32, _c_i32, _c_i32, _c_p]),
     "sdb_paged_attention_readonly": (_c_i32, [
         _c_p, _c_i64, _c_i64, _c_p, _c_p, _c_i64, _c_i64, _c_i64, _c_p, _c_i64, _c_p,
         _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32,
