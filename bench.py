@@ -353,6 +353,116 @@ def run_ours(args):
     return 0
 
 
+
+# --------------------------------------------------------------------------- side modes
+def _time_events(fn, steps, warmup, per_graph=20):
+    """Device ms per call: ``per_graph`` calls captured in one CUDA graph, replayed so that
+    short kernels are timed back to back instead of at the host's launch rate."""
+    import torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    st = torch.cuda.Stream()
+    st.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(st):
+        with torch.cuda.graph(g, stream=st):
+            for _ in range(per_graph):
+                fn()
+    torch.cuda.current_stream().wait_stream(st)
+    g.replay()
+    torch.cuda.synchronize()
+    reps = max(1, steps // per_graph)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    del g
+    return e0.elapsed_time(e1) / (reps * per_graph)
+
+
+def run_side(args):
+    """Secondary kernels of the path, one JSON line each (single GPU)."""
+    import numpy as np
+    import torch
+    torch.cuda.set_device(0)
+    pkg = load_package()
+    from specdec_nanovllm_b200 import workloads
+    peak, peak_kind = measured_peak()
+    steps = min(args.steps, 500)
+    if args.mode == "verify_batch":
+        from oracle.verify import algorithmic_bytes
+        B, k, V = 64, 6, workloads.VOCAB
+        draft, target, tokens = workloads.cfg4_inputs(B=B, k=k, V=V, seed=0)
+        temps = torch.ones(B, device="cuda")
+        res = pkg.verify_batch(draft, target, tokens, temps, seed=1, offset=0)
+        ms = _time_events(lambda: pkg.verify_batch(draft, target, tokens, temps, seed=1, offset=0, out=res),
+                          steps, args.warmup)
+        nbytes = algorithmic_bytes(B, k, V)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        line = {"metric": "verify_batch HBM GB/s", "value": round(gbs, 2), "unit": "GB/s", "n_gpus": 1,
+                "steps": steps, "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
+                "dtype": "f32", "data": "synthetic",
+                "config": {"workload": f"verify_batch B={B} k={k} V={V} (target N(0,9), draft = target + N(0,1), "
+                                       "T=1, in-kernel Philox draws)", "bytes_per_step": nbytes},
+                "roofline": {"bound": "hbm", "achieved": round(gbs, 2), "peak": peak, "peak_kind": peak_kind,
+                             "unit": "GB/s", "frac": round(gbs / peak, 4),
+                             "note": "whole call (3 launches) against one read of every logit"},
+                "gpu_launches": 3 * steps}
+    elif args.mode == "w8a16":
+        from oracle.quant import algorithmic_bytes
+        M = args.m
+        shapes = workloads.W8A16_SHAPES
+        ins = {n: workloads.cfg3_inputs(M, K, N, seed=i) for i, (n, (K, N)) in enumerate(shapes.items())}
+        outs = {n: pkg.int8_linear(*ins[n]) for n in ins}
+
+        def step():
+            for n in ins:
+                pkg.int8_linear(*ins[n], out=outs[n])
+        ms = _time_events(step, steps, args.warmup)
+        per = {}
+        for n in ins:
+            ms_n = _time_events(lambda n=n: pkg.int8_linear(*ins[n], out=outs[n]), steps, args.warmup)
+            K, N = shapes[n]
+            b = algorithmic_bytes(M, N, K)
+            per[n] = {"us": round(ms_n * 1e3, 2), "GB/s": round(b / (ms_n * 1e-3) / 1e9, 1),
+                      "TFLOP/s": round(2 * M * N * K / (ms_n * 1e-3) / 1e12, 2)}
+        nbytes = sum(algorithmic_bytes(M, N, K) for K, N in shapes.values())
+        flops = sum(2 * M * N * K for K, N in shapes.values())
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        line = {"metric": "w8a16 HBM GB/s (4 Qwen3-4B projections)", "value": round(gbs, 2), "unit": "GB/s",
+                "n_gpus": 1, "steps": steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
+                "higher_is_better": True, "dtype": "fp16 x int8", "data": "synthetic",
+                "config": {"workload": f"int8_linear M={M} over qkv/o/gate_up/down", "per_projection": per,
+                           "bytes_per_step": nbytes, "flops_per_step": flops},
+                "roofline": {"bound": "hbm", "achieved": round(gbs, 2), "peak": peak, "peak_kind": peak_kind,
+                             "unit": "GB/s", "frac": round(gbs / peak, 4),
+                             "tflops": round(flops / (ms * 1e-3) / 1e12, 2)},
+                "gpu_launches": 4 * steps}
+    else:  # decode attention
+        from oracle.attention import algorithmic_bytes
+        B, L = B_PER_GPU, CTX
+        case = workloads.paged_case([L] * B, 1, device="cuda", seed=3, extra_blocks=0, generate_on_device=True,
+                                    **workloads.QWEN3_4B)
+        out = torch.empty_like(case.q)
+        fn = lambda: pkg.paged_attention(case.q, case.k_cache, case.v_cache, case.block_tables,
+                                         case.cache_seqlens, case.scale, n_q=1, out=out)
+        ms = _time_events(fn, steps, args.warmup)
+        nbytes = algorithmic_bytes([L] * B, 1, HQ, HKV, D, 2, 2)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        line = {"metric": "decode-attn HBM GB/s", "value": round(gbs, 2), "unit": "GB/s", "n_gpus": 1,
+                "steps": steps, "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
+                "dtype": "bf16", "data": "synthetic",
+                "config": {"workload": f"decode-attn B={B} ctx={L} (Qwen3-4B heads)", "bytes_per_step": nbytes},
+                "roofline": {"bound": "hbm", "achieved": round(gbs, 2), "peak": peak, "peak_kind": peak_kind,
+                             "unit": "GB/s", "frac": round(gbs / peak, 4)},
+                "gpu_launches": steps}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -360,10 +470,16 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--skip-cpu", action="store_true", help="omit the CPU baseline leg")
+    ap.add_argument("--mode", choices=["verify_attn", "decode_attn", "verify_batch", "w8a16"],
+                    default="verify_attn", help="verify_attn is the headline; the others measure the "
+                    "secondary kernels of the path on one GPU")
+    ap.add_argument("--m", type=int, default=1, help="tokens (M) for --mode w8a16")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         return run_reference(args)
+    if args.mode != "verify_attn":
+        return run_side(args)
     return run_ours(args)
 
 

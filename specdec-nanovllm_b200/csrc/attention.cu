@@ -34,72 +34,14 @@
 // bottom of this file.
 #include <cfloat>
 #include <cstdio>
+#include <cstdlib>
+#include <cstring>
 #include <type_traits>
 
-#include "common.cuh"
+#include "attention_common.cuh"
 
 namespace sdb {
 namespace attn {
-
-constexpr int D = 128;
-constexpr int BN = 64;                 // keys per stage
-constexpr int HALF_BYTES = BN * 128;   // one 64-dim half of a K or V tile (8 KB, swizzled)
-constexpr int TILE_BYTES = 2 * HALF_BYTES;
-constexpr int STAGE_BYTES = 2 * TILE_BYTES;  // K + V
-constexpr float NEG_INF = -INFINITY;
-
-struct Params {
-    const void* q;
-    int64_t q_srow, q_shead;
-    void* out;
-    int64_t o_srow, o_shead;
-    const int* bt;
-    int64_t bt_stride;
-    const int* seqlens;
-    float* part_o;   // [B*Hkv*splits][R][D]
-    float* part_ml;  // [B*Hkv*splits][R][2]
-    int* counters;   // [B*Hkv]
-    int* err;
-    unsigned* checksum;  // read-only twin only
-    int B, n_q, G, R, Hkv, page, max_blocks, num_blocks, splits, chunk;
-    float scale_log2;
-};
-
-struct WsLayout {
-    size_t err, counters, part_ml, part_o, total;
-};
-
-// The split-merge counters live at a fixed offset with a fixed capacity, so one
-// workspace can serve calls of any shape in any order: a counter slot is never
-// aliased by another call's partials, and every kernel leaves its counters at 0.
-constexpr int kCounterCap = 65536;  // (sequence, kv head) pairs
-
-static WsLayout ws_layout(int B, int R, int Hkv, int splits) {
-    WsLayout w;
-    size_t off = 0;
-    w.err = off;
-    off += 256;
-    w.counters = off;
-    off = align_up(off + sizeof(int) * (size_t)kCounterCap, 256);
-    const size_t slots = (size_t)B * Hkv * (splits > 1 ? splits : 0);
-    w.part_ml = off;
-    off = align_up(off + sizeof(float) * slots * R * 2, 256);
-    w.part_o = off;
-    off = align_up(off + sizeof(float) * slots * R * D, 256);
-    w.total = off;
-    return w;
-}
-
-// Sequence length clamped to the table capacity, error bit on violation.
-SDB_DEV int load_len(const Params& p, int b) {
-    int L = p.seqlens[b];
-    const int cap = p.max_blocks * p.page;
-    if (L < 0 || L > cap) {
-        if (threadIdx.x == 0) atomicOr(p.err, SDB_KERR_SEQLEN);
-        L = L < 0 ? 0 : cap;
-    }
-    return L;
-}
 
 // Producer: stream the tiles of [k0, k0 + ntiles*BN) for (b, kvh) into the ring.
 template <int NS, int NCONS_PER_STAGE>
@@ -684,7 +626,6 @@ template <int MT>
 struct Stages {
     static constexpr int NS = 3;
 };
-constexpr int kMaxStages = 3;
 constexpr int kSmemPerSM = 233472;  // 228 KB on sm_100
 // splits x R (<= 64) fp32 merge coefficients must fit the smallest stage ring (64 KB)
 constexpr int kMaxSplits = 256;
@@ -733,10 +674,17 @@ static int pick_splits(int B, int R, int Hkv, int page, int max_blocks, int sms)
 using namespace sdb;
 using namespace sdb::attn;
 
+bool sdb::attn::prefer_umma() {
+    const char* v = getenv("SDB_ATTN_KERNEL");
+    return !(v && strcmp(v, "mma") == 0);
+}
+
 extern "C" int sdb_paged_attention_default_splits(int B, int n_q, int Hq, int Hkv, int D_, int page,
                                                   int max_blocks, int dtype) {
     if (B <= 0 || n_q <= 0 || Hkv <= 0 || Hq % Hkv != 0 || page <= 0 || max_blocks <= 0) return 1;
     const int R = n_q * (Hq / Hkv);
+    if (umma_path(dtype, D_, page, R) && prefer_umma())
+        return pick_umma_splits(B, R, Hkv, page, max_blocks, device_sm_count());
     if (!mma_path(dtype, D_, page, R)) return 1;
     return pick_splits(B, R, Hkv, page, max_blocks, device_sm_count());
 }
@@ -872,6 +820,21 @@ extern "C" int sdb_paged_attention(const void* q, int64_t q_srow, int64_t q_shea
     p.max_blocks = max_blocks;
     p.num_blocks = num_blocks;
     p.scale_log2 = softmax_scale * 1.4426950408889634f;
+
+    if (umma_path(dtype, D_, page, R) && prefer_umma()) {
+        if ((long long)B * Hkv > kCounterCap) {
+            set_last_error("B * Hkv = %lld exceeds the supported %d (sequence, kv head) pairs", (long long)B * Hkv,
+                           kCounterCap);
+            return SDB_ERR_UNSUPPORTED;
+        }
+        if ((reinterpret_cast<uintptr_t>(q) & 15) || (q_srow % 8) || (q_shead % 8) ||
+            (reinterpret_cast<uintptr_t>(k_cache) & 15) || (reinterpret_cast<uintptr_t>(v_cache) & 15) ||
+            ((sh * 2) & 15) || ((sp * 2) & 15) || ((sb * 2) & 15)) {
+            set_last_error("q rows and the KV cache must be 16-byte aligned");
+            return SDB_ERR_INVALID_ARG;
+        }
+        return launch_umma(k_cache, v_cache, dtype, sb, sp, sh, p, workspace, workspace_bytes, splits, st);
+    }
 
     if (mma_path(dtype, D_, page, R)) {
         if (splits <= 0) splits = pick_splits(B, R, Hkv, page, max_blocks, device_sm_count());

@@ -29,6 +29,17 @@ def _check(got, want, tol):
     assert ok, f"max abs err {err}, worst violation {viol}"
 
 
+@pytest.fixture(autouse=True, params=["auto", "mma"])
+def kernel_choice(request, monkeypatch):
+    """Every test runs on the default kernel (tcgen05 where the shape allows) and on
+    the mma.sync kernel (SDB_ATTN_KERNEL=mma)."""
+    if request.param == "mma":
+        monkeypatch.setenv("SDB_ATTN_KERNEL", "mma")
+    else:
+        monkeypatch.delenv("SDB_ATTN_KERNEL", raising=False)
+    return request.param
+
+
 @pytest.fixture(scope="module")
 def W(pkg):
     from specdec_nanovllm_b200 import workloads
