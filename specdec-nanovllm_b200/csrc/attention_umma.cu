@@ -10,19 +10,20 @@
 //   S^T[key, row] = K[key, :] . Q[row, :]        M = 128 keys, N = 32 rows, K = 128 dims
 //   O^T[dim, row] += V^T[dim, key] . P^T[key, row] M = 128 dims, N = 32 rows, K = 128 keys
 // Both accumulators live in tensor memory (TMEM): S^T double-buffered in
-// columns [0, 64), O^T in [64, 96).  K and V tiles arrive by TMA in the
+// columns [0, 64), O^T head / residual parts in [64, 96) / [96, 128).  K and V tiles arrive by TMA in the
 // 128-byte-swizzled layout the MMA descriptors read directly (K as a K-major A
 // operand, V as an MN-major A operand); Q^T and P^T are written by the softmax
 // warps as K-major B operands.  P is split into a 16-bit head and a 16-bit
 // residual and both multiply V, so the probabilities keep ~16 significant bits.
 //
-// Warp roles (192 threads, one CTA per SM, persistent over work items):
+// Warp roles (320 threads, one CTA per SM, persistent over work items):
 //   warp 0      TMA producer: K/V tiles of 128 keys into a 3-stage ring
 //   warp 1      TMEM owner and MMA issuer (one thread)
-//   warps 2..5  softmax: thread = one TMEM lane (a key of S^T, a dim of O^T);
-//               column max / sum by an in-warp transpose reduction + a 4-warp
-//               exchange; lazy rescale (O is rescaled only when a row max grows
-//               by more than 2^8, exact because the reference point is kept).
+//   warps 2..9  softmax: thread = one TMEM lane (a key of S^T, a dim of O^T) and
+//               16 of the 32 columns (rows); column max / sum by an in-warp
+//               transpose reduction + a 4-warp exchange; lazy rescale (O is
+//               rescaled only when a row max grows by more than 2^8, exact
+//               because the reference point is kept).
 // Work items (split, kv head, sequence) are strided over the persistent CTAs;
 // the producer streams the next item's tiles while the current one finishes.
 // Every wait is bounded and reports SDB_KERR_TIMEOUT instead of hanging.
@@ -42,22 +43,30 @@ constexpr int USTAGE = 2 * UTILE;         // K + V: 64 KB
 constexpr int UNS = 3;                    // stages
 constexpr int NROW = 32;                  // MMA N: query rows per (sequence, kv head)
 constexpr int QHALF = NROW * 128;         // 4 KB
-constexpr int PHALF = NROW * 128;         // 4 KB (64 keys of 32 rows)
-constexpr int OFF_Q = UNS * USTAGE;
-constexpr int OFF_PHI = OFF_Q + 2 * QHALF;
-constexpr int OFF_PLO = OFF_PHI + 2 * PHALF;
-constexpr int OFF_RED = OFF_PLO + 2 * PHALF;          // red_max[4][32], red_sum[4][32]
-constexpr int OFF_BAR = OFF_RED + 2 * 4 * 32 * 4;
-// barriers: full[3] empty[3] s_full[2] s_free[2] p_full o_done q_ready fin
+// P^T of tile t is written into the K half of tile t's stage once S(t) has read K,
+// as one N = 64 B operand: rows 0..31 are the 16-bit heads of P^T's 32 columns,
+// rows 32..63 their residuals, so a single MMA per key step reads V once and
+// accumulates O_head and O_residual side by side (64 TMEM columns).  Two key halves
+// of 64 rows x 128 B.  The stage ring thus multi-buffers P and the P.V completion
+// that frees the stage also frees P.
+constexpr int PROWS = 2 * NROW;
+constexpr int PKHALF = PROWS * 128;       // 8 KB
+constexpr int QBUF = 2 * QHALF;           // one item's Q^T (8 KB)
+constexpr int OFF_Q = UNS * USTAGE;       // two Q^T buffers: item i uses buffer i & 1
+constexpr int OFF_RED = OFF_Q + 2 * QBUF;             // red_max[4][32], red_sum[4][32]
+constexpr int kMaxUmmaSplits = 16;
+constexpr int OFF_W = OFF_RED + 2 * 4 * 32 * 4;       // merge weights [splits][32] + 1/L [32]
+constexpr int OFF_BAR = OFF_W + (kMaxUmmaSplits + 1) * 32 * 4;
+// barriers: full[3] empty[3] s_full[2] s_free[2] p_full q_ready[2] fin
 constexpr int NBAR = UNS * 2 + 2 + 2 + 4;
 constexpr int OFF_TMEM = OFF_BAR + NBAR * 8;
 constexpr int SMEM_BYTES = OFF_TMEM + 16 + 1024;  // + alignment slack
-constexpr int kMaxUmmaSplits = 16;
 constexpr uint32_t TMEM_COLS = 128;
-constexpr int THREADS = 192;
+constexpr int SOFTMAX_THREADS = 256;  // 8 warps
+constexpr int THREADS = 64 + SOFTMAX_THREADS;
 
 struct Bars {
-    uint32_t full0, empty0, sfull0, sfree0, pfull, odone, qready, fin;
+    uint32_t full0, empty0, sfull0, sfree0, pfull, qready0, fin;
 };
 
 SDB_DEV Bars bars_at(uint32_t base) {
@@ -67,9 +76,8 @@ SDB_DEV Bars bars_at(uint32_t base) {
     b.sfull0 = base + 16 * UNS;
     b.sfree0 = b.sfull0 + 16;
     b.pfull = b.sfree0 + 16;
-    b.odone = b.pfull + 8;
-    b.qready = b.odone + 8;
-    b.fin = b.qready + 8;
+    b.qready0 = b.pfull + 8;
+    b.fin = b.qready0 + 16;
     return b;
 }
 
@@ -99,11 +107,12 @@ SDB_DEV bool wait_or_skip(uint32_t bar, uint32_t parity, bool& ok) {
     return ok;
 }
 
-// In-warp transpose reduction: lane c ends with op over the 32 lanes of v[c].
+// In-warp transpose reduction of 16 columns: lanes c and c + 16 end with op over
+// the 32 lanes of v[c] (16 + 4 + ... shuffles instead of 16 x 5).
 template <bool MAX>
-SDB_DEV float transpose_reduce(float (&v)[32], int lane) {
+SDB_DEV float transpose_reduce16(float (&v)[16], int lane) {
 #pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) {
+    for (int off = 8; off >= 1; off >>= 1) {
         const bool upper = (lane & off) != 0;
 #pragma unroll
         for (int i = 0; i < off; ++i) {
@@ -113,7 +122,39 @@ SDB_DEV float transpose_reduce(float (&v)[32], int lane) {
             v[i] = MAX ? fmaxf(keep, recv) : keep + recv;
         }
     }
-    return v[0];
+    const float other = __shfl_xor_sync(0xffffffffu, v[0], 16);
+    return MAX ? fmaxf(v[0], other) : v[0] + other;
+}
+
+// Q^T of item `it` into Q buffer `buf` as a K-major swizzled B operand (rows >= R zero),
+// then release it to the MMA warp.  Called by the 256 softmax threads.
+template <typename T>
+SDB_DEV void write_q(const Params& p, uint8_t* smem, int it, int buf, int st, const Bars& bar) {
+    const Item x = item_at(p, it);
+    const T* qbase = reinterpret_cast<const T*>(p.q);
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        const int u = st + SOFTMAX_THREADS * i;
+        const int c = u >> 4, chk = u & 15;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (c < p.R) {
+            const int r = c / p.G, g = c % p.G;
+            v = __ldg(reinterpret_cast<const uint4*>(qbase + (int64_t)(x.b * p.n_q + r) * p.q_srow +
+                                                     (int64_t)(x.kvh * p.G + g) * p.q_shead + chk * 8));
+        }
+        *reinterpret_cast<uint4*>(smem + OFF_Q + buf * QBUF + (chk >> 3) * QHALF + c * 128 +
+                                  (((chk & 7) ^ (c & 7)) << 4)) = v;
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    mbar_arrive(bar.qready0 + 8 * buf);
+}
+
+// Next work item of this CTA after `it` that has at least one tile (or total_items).
+SDB_DEV int next_busy_item(const Params& p, int it, int total_items) {
+    for (it += gridDim.x; it < total_items; it += gridDim.x)
+        if (item_at(p, it).ntiles > 0) return it;
+    return total_items;
 }
 
 template <typename T>
@@ -139,11 +180,11 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(bar.sfull0 + 8 * i, 1);
-            mbar_init(bar.sfree0 + 8 * i, 128);
+            mbar_init(bar.sfree0 + 8 * i, SOFTMAX_THREADS);
         }
-        mbar_init(bar.pfull, 128);
-        mbar_init(bar.odone, 1);
-        mbar_init(bar.qready, 128);
+        mbar_init(bar.pfull, SOFTMAX_THREADS);
+        mbar_init(bar.qready0, SOFTMAX_THREADS);
+        mbar_init(bar.qready0 + 8, SOFTMAX_THREADS);
         mbar_init(bar.fin, 1);
         fence_mbarrier_init();
     }
@@ -203,30 +244,29 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (lane == 0) {
             constexpr bool BF = std::is_same<T, __nv_bfloat16>::value;
             constexpr uint32_t IDESC_S = idesc_f16(BF, false, false, 128, NROW);
-            constexpr uint32_t IDESC_PV = idesc_f16(BF, true, false, 128, NROW);
+            constexpr uint32_t IDESC_PV = idesc_f16(BF, true, false, 128, PROWS);
             int gt = 0, nitem = 0;
             bool ok = true;
+            // O^T += V(g)^T . P^T(g), head then residual; completion frees stage g (K, V and P)
             auto pv = [&](int g, bool first) -> bool {
                 if (!mbar_wait(bar.pfull, g & 1)) return false;
                 tc_fence_after();
-                const uint32_t vbase = sbase + (g % UNS) * USTAGE + UTILE;
+                const uint32_t stage = sbase + (g % UNS) * USTAGE;
+                const uint32_t vbase = stage + UTILE;
 #pragma unroll
-                for (int part = 0; part < 2; ++part) {
-                    const uint32_t pbase = sbase + (part == 0 ? OFF_PHI : OFF_PLO);
-#pragma unroll
-                    for (int ks = 0; ks < 8; ++ks) {
-                        const uint64_t a = sdesc_sw128(vbase + ks * 2048, UHALF, 1024);
-                        const uint64_t b = sdesc_sw128(pbase + (ks >> 2) * PHALF + (ks & 3) * 32, 16, 1024);
-                        umma_f16_ss(tmem + 64, a, b, IDESC_PV, (first && part == 0 && ks == 0) ? 0u : 1u);
-                    }
+                for (int ks = 0; ks < 8; ++ks) {
+                    const uint64_t a = sdesc_sw128(vbase + ks * 2048, UHALF, 1024);
+                    const uint64_t b = sdesc_sw128(stage + (ks >> 2) * PKHALF + (ks & 3) * 32, 16, 1024);
+                    umma_f16_ss(tmem + 64, a, b, IDESC_PV, (first && ks == 0) ? 0u : 1u);
                 }
-                umma_commit(bar.odone);
                 umma_commit(bar.empty0 + 8 * (g % UNS));
                 return true;
             };
-            for (int it = blockIdx.x; it < total_items && ok; it += gridDim.x, ++nitem) {
+            // nitem counts the items that have tiles: only those take a Q buffer / q_ready phase
+            for (int it = blockIdx.x; it < total_items && ok; it += gridDim.x) {
                 const Item x = item_at(p, it);
-                if (!mbar_wait(bar.qready, nitem & 1)) {
+                if (x.ntiles == 0) continue;
+                if (!mbar_wait(bar.qready0 + 8 * (nitem & 1), (nitem >> 1) & 1)) {
                     ok = false;
                     break;
                 }
@@ -243,7 +283,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                     for (int ks = 0; ks < 8; ++ks) {
                         const uint64_t a = sdesc_sw128(kbase + (ks >> 2) * UHALF + (ks & 3) * 32, 16, 1024);
-                        const uint64_t b = sdesc_sw128(sbase + OFF_Q + (ks >> 2) * QHALF + (ks & 3) * 32, 16, 1024);
+                        const uint64_t b =
+                            sdesc_sw128(sbase + OFF_Q + (nitem & 1) * QBUF + (ks >> 2) * QHALF + (ks & 3) * 32, 16, 1024);
                         umma_f16_ss(tmem + sb * 32, a, b, IDESC_S, ks > 0 ? 1u : 0u);
                     }
                     umma_commit(bar.sfull0 + 8 * sb);
@@ -252,7 +293,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                         break;
                     }
                 }
-                if (ok && x.ntiles >= 1 && !pv(gt - 1, x.ntiles == 1)) ok = false;
+                if (ok && !pv(gt - 1, x.ntiles == 1)) ok = false;
+                ++nitem;
             }
             if (!ok) atomicOr(p.err, SDB_KERR_TIMEOUT);
             // every MMA this thread issued has completed before TMEM is released
@@ -261,136 +303,156 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
     } else {
         // ------------------------------------------------------------- softmax warps
-        const int st = threadIdx.x - 64;   // 0..127
-        const int qt = warp & 3;           // TMEM lane quarter of this warp
+        // 8 warps: warp w (2..9) reads TMEM lane quarter qt = w % 4 (its 32 keys of S^T,
+        // its 32 dims of O^T) and column half ch = (w - 2) / 4 (16 of the 32 rows).
+        //
+        // Common path per tile: no reduction at all.  Every thread keeps the reference
+        // point mbv[i] of each of its 16 rows; if no logit of the tile exceeds its row's
+        // reference by more than 8 (log2 units, p <= 256), one vote barrier confirms it,
+        // P = 2^(x - ref) is written and the row sums accumulate per thread.  Otherwise
+        // (first tile of an item, or a row max that grew) all warps take the exact path:
+        // column max over the 128 keys, new reference = max, partial sums and O rescaled.
+        const int sw = warp - 2;            // 0..7
+        const int st = threadIdx.x - 64;    // 0..255
+        const int qt = warp & 3;
+        const int ch = sw >> 2;
+        const int c0 = 16 * ch;             // first column (row) of this thread
+        const int lc = lane & 15;           // column whose reference this lane owns: c0 + lc
         const uint32_t lane_addr = (uint32_t)(32 * qt) << 16;
         const int R = p.R;
         const float sl2 = p.scale_log2;
         int gt = 0;
         bool ok = true;
         T* obase = reinterpret_cast<T*>(p.out);
-        const T* qbase = reinterpret_cast<const T*>(p.q);
+        // Q^T buffers: the i-th item with tiles uses buffer i & 1; the next one is written
+        // while the current one runs, so the MMA warp starts an item without waiting.
+        int qi = 0;
+        {
+            const int first = item_at(p, blockIdx.x < total_items ? blockIdx.x : 0).ntiles > 0
+                                  ? blockIdx.x
+                                  : next_busy_item(p, blockIdx.x, total_items);
+            if (blockIdx.x < total_items && first < total_items) write_q<T>(p, smem, first, 0, st, bar);
+        }
         for (int it = blockIdx.x; it < total_items; it += gridDim.x) {
             const Item x = item_at(p, it);
-            // ---- Q^T of this item into the K-major swizzled B operand (rows >= R are zero)
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                const int u = st + 128 * i;
-                const int c = u >> 4, ch = u & 15;
-                uint4 v = make_uint4(0, 0, 0, 0);
-                if (c < R) {
-                    const int r = c / p.G, g = c % p.G;
-                    v = __ldg(reinterpret_cast<const uint4*>(qbase + (int64_t)(x.b * p.n_q + r) * p.q_srow +
-                                                             (int64_t)(x.kvh * p.G + g) * p.q_shead + ch * 8));
-                }
-                *reinterpret_cast<uint4*>(smem + OFF_Q + (ch >> 3) * QHALF + c * 128 + (((ch & 7) ^ (c & 7)) << 4)) =
-                    v;
+            if (x.ntiles > 0) {
+                const int nxt = next_busy_item(p, it, total_items);
+                if (nxt < total_items) write_q<T>(p, smem, nxt, (qi + 1) & 1, st, bar);
+                ++qi;
             }
-            fence_proxy_async_smem();
-            tc_fence_before();
-            mbar_arrive(bar.qready);
 
-            // per-row (column) softmax state, held by lane c of every softmax warp
-            float mb = NEG_INF, lsum = 0.f;
+            float mb_own = NEG_INF;   // reference of column c0 + lc
+            float mbv[16], lpart[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                mbv[i] = NEG_INF;
+                lpart[i] = 0.f;
+            }
             const int lbase = x.L - p.n_q + 1;  // keys visible to row r: j < lbase + r
             for (int t = 0; t < x.ntiles; ++t, ++gt) {
                 const int sb = gt & 1, s = gt % UNS;
                 const int j0 = x.k0 + t * UBN;
                 wait_or_skip(bar.sfull0 + 8 * sb, (gt >> 1) & 1, ok);
                 tc_fence_after();
-                uint32_t sr[32];
-                tmem_ld32(tmem + lane_addr + sb * 32, sr);
+                uint32_t sr[16];
+                tmem_ld16(tmem + lane_addr + sb * 32 + c0, sr);
                 tmem_wait_ld();
                 tc_fence_before();
                 mbar_arrive(bar.sfree0 + 8 * sb);
 
                 const int key = j0 + 32 * qt + lane;
-                const bool masked = (j0 + UBN > min(lbase, x.k1)) || R < NROW;
-                float xv[32];
-                {
-                    int r = 0, g = 0;
+                float xv[16];
+                if (j0 + UBN > min(lbase, x.k1)) {
+                    // tail tile: causal limits, split end, pad rows
+                    int r = c0 / p.G, g = c0 % p.G;
 #pragma unroll
-                    for (int c = 0; c < 32; ++c) {
-                        float v = __uint_as_float(sr[c]) * sl2;
-                        if (masked) {
-                            const bool vis = c < R && key < min(lbase + r, x.k1);
-                            v = vis ? v : NEG_INF;
-                            if (++g == p.G) {
-                                g = 0;
-                                ++r;
-                            }
+                    for (int i = 0; i < 16; ++i) {
+                        const bool vis = c0 + i < R && key < min(lbase + r, x.k1);
+                        xv[i] = vis ? __uint_as_float(sr[i]) * sl2 : NEG_INF;
+                        if (++g == p.G) {
+                            g = 0;
+                            ++r;
                         }
-                        xv[c] = v;
                     }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) xv[i] = __uint_as_float(sr[i]) * sl2;
                 }
-                // column max over the tile's 128 keys
-                float tmp[32];
+                bool need = false;
 #pragma unroll
-                for (int c = 0; c < 32; ++c) tmp[c] = xv[c];
-                red_max[qt * 32 + lane] = transpose_reduce<true>(tmp, lane);
-                named_barrier_sync(1, 128);
-                const float M = fmaxf(fmaxf(red_max[lane], red_max[32 + lane]),
-                                      fmaxf(red_max[64 + lane], red_max[96 + lane]));
-                // lazy rescale: move the reference point only when the max grows by > 2^8
-                const float nb = (M > mb + 8.0f) ? M : mb;
-                const float alpha = (nb != mb) ? ex2(mb - nb) : 1.0f;
-                const bool rescale = __any_sync(0xffffffffu, nb != mb && lsum > 0.f);
-                mb = nb;
-                float pv[32];
+                for (int i = 0; i < 16; ++i) need |= xv[i] > mbv[i] + 8.0f;
+                if (barrier_or(1, SOFTMAX_THREADS, need)) {
+                    // exact path (uniform over the 8 warps)
+                    float tmp[16];
 #pragma unroll
-                for (int c = 0; c < 32; ++c) {
-                    const float mc = __shfl_sync(0xffffffffu, mb, c);
-                    pv[c] = ex2(xv[c] - (mc == NEG_INF ? 0.f : mc));
-                }
+                    for (int i = 0; i < 16; ++i) tmp[i] = xv[i];
+                    const float wm = transpose_reduce16<true>(tmp, lane);
+                    if (lane < 16) red_max[qt * 32 + c0 + lane] = wm;
+                    named_barrier_sync(1, SOFTMAX_THREADS);
+                    const int cc = c0 + lc;
+                    const float M =
+                        fmaxf(fmaxf(red_max[cc], red_max[32 + cc]), fmaxf(red_max[64 + cc], red_max[96 + cc]));
+                    const float nb = fmaxf(M, mb_own);
+                    const float alpha = nb == mb_own ? 1.0f : ex2(mb_own - nb);
+                    mb_own = nb;
+                    float av[16];
 #pragma unroll
-                for (int c = 0; c < 32; ++c) tmp[c] = pv[c];
-                red_sum[qt * 32 + lane] = transpose_reduce<false>(tmp, lane);
-                named_barrier_sync(1, 128);
-                lsum = lsum * alpha + (red_sum[lane] + red_sum[32 + lane]) + (red_sum[64 + lane] + red_sum[96 + lane]);
-
-                // the previous tile's P.V has finished: P buffer free, O up to date
-                if (t >= 1) {
-                    wait_or_skip(bar.odone, (gt - 1) & 1, ok);
-                    tc_fence_after();
-                    if (rescale) {
-                        uint32_t orr[32];
-                        tmem_ld32(tmem + lane_addr + 64, orr);
+                    for (int i = 0; i < 16; ++i) {
+                        mbv[i] = __shfl_sync(0xffffffffu, mb_own, i);
+                        av[i] = __shfl_sync(0xffffffffu, alpha, i);
+                        lpart[i] *= av[i];
+                    }
+                    if (t >= 1) {
+                        // P.V(t-1) complete (it frees stage t-1): O is up to date, rescale it
+                        const int g1 = gt - 1;
+                        wait_or_skip(bar.empty0 + 8 * (g1 % UNS), (g1 / UNS) & 1, ok);
+                        tc_fence_after();
+                        uint32_t oh[16], ol[16];
+                        tmem_ld16(tmem + lane_addr + 64 + c0, oh);
+                        tmem_ld16(tmem + lane_addr + 96 + c0, ol);
                         tmem_wait_ld();
 #pragma unroll
-                        for (int c = 0; c < 32; ++c) {
-                            const float a = __shfl_sync(0xffffffffu, alpha, c);
-                            orr[c] = __float_as_uint(__uint_as_float(orr[c]) * a);
+                        for (int i = 0; i < 16; ++i) {
+                            oh[i] = __float_as_uint(__uint_as_float(oh[i]) * av[i]);
+                            ol[i] = __float_as_uint(__uint_as_float(ol[i]) * av[i]);
                         }
-                        tmem_st32(tmem + lane_addr + 64, orr);
+                        tmem_st16(tmem + lane_addr + 64 + c0, oh);
+                        tmem_st16(tmem + lane_addr + 96 + c0, ol);
                         tmem_wait_st();
                     }
                 }
+                float pv[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    pv[i] = ex2(xv[i] - (mbv[i] == NEG_INF ? 0.f : mbv[i]));
+                    lpart[i] += pv[i];
+                }
                 // keys past the split end: zero their V rows (unwritten cache may hold NaN)
                 const int kin = 32 * qt + lane;
+                uint8_t* stage = smem + s * USTAGE;
                 if (j0 + UBN > x.k1) {
                     wait_or_skip(bar.full0 + 8 * s, (gt / UNS) & 1, ok);
                     if (j0 + kin >= x.k1) {
-                        uint8_t* vrow = smem + s * USTAGE + UTILE + kin * 128;
+                        uint8_t* vrow = stage + UTILE + kin * 128 + ch * UHALF;
 #pragma unroll
-                        for (int h = 0; h < 2; ++h)
-#pragma unroll
-                            for (int cc = 0; cc < 8; ++cc)
-                                *reinterpret_cast<uint4*>(vrow + h * UHALF + cc * 16) = make_uint4(0, 0, 0, 0);
+                        for (int q16 = 0; q16 < 8; ++q16)
+                            *reinterpret_cast<uint4*>(vrow + q16 * 16) = make_uint4(0, 0, 0, 0);
                     }
                 }
-                // P^T (head and residual) into the K-major swizzled B operands
+                // P^T (heads in rows 0..31, residuals in rows 32..63) into the K half of this
+                // stage (S(t) has read K); row r of a key half sits at r*128, chunk ^ (r & 7)
                 {
                     const int half = kin >> 6, kk = kin & 63;
                     const int chunk = kk >> 3, byte = (kk & 7) * 2;
-                    uint8_t* phi = smem + OFF_PHI + half * PHALF + byte;
-                    uint8_t* plo = smem + OFF_PLO + half * PHALF + byte;
+                    uint8_t* pb = stage + half * PKHALF + byte;
 #pragma unroll
-                    for (int c = 0; c < 32; ++c) {
-                        const uint32_t packed = H::pack(pv[c], 0.f);
-                        const uint32_t resid = H::pack_residual(pv[c], 0.f, packed);
+                    for (int i = 0; i < 16; ++i) {
+                        const int c = c0 + i;
+                        uint16_t hi, lo;
+                        H::split(pv[i], hi, lo);
                         const int o = c * 128 + ((chunk ^ (c & 7)) << 4);
-                        *reinterpret_cast<uint16_t*>(phi + o) = (uint16_t)(packed & 0xffffu);
-                        *reinterpret_cast<uint16_t*>(plo + o) = (uint16_t)(resid & 0xffffu);
+                        *reinterpret_cast<uint16_t*>(pb + o) = hi;
+                        *reinterpret_cast<uint16_t*>(pb + o + NROW * 128) = lo;  // row c + 32: same swizzle
                     }
                 }
                 fence_proxy_async_smem();
@@ -398,30 +460,43 @@ __global__ void __launch_bounds__(THREADS, 1)
                 mbar_arrive(bar.pfull);
             }
 
-            // ---- item epilogue: O^T column c is row c; this thread holds dim 32*qt + lane
-            float o[32];
+            // ---- item epilogue: row sums, then O^T column c is row c (this thread: dim 32*qt + lane)
+            float lsum;
+            {
+                const float ws = transpose_reduce16<false>(lpart, lane);
+                // every warp has read the previous item's red_sum (an item without tiles
+                // reaches this point with no vote barrier in between)
+                named_barrier_sync(1, SOFTMAX_THREADS);
+                if (lane < 16) red_sum[qt * 32 + c0 + lane] = ws;
+                named_barrier_sync(1, SOFTMAX_THREADS);
+                const int cc = c0 + lc;
+                lsum = (red_sum[cc] + red_sum[32 + cc]) + (red_sum[64 + cc] + red_sum[96 + cc]);
+            }
+            float o[16];
             if (x.ntiles > 0) {
-                wait_or_skip(bar.odone, (gt - 1) & 1, ok);
+                const int g1 = gt - 1;
+                wait_or_skip(bar.empty0 + 8 * (g1 % UNS), (g1 / UNS) & 1, ok);
                 tc_fence_after();
-                uint32_t orr[32];
-                tmem_ld32(tmem + lane_addr + 64, orr);
+                uint32_t oh[16], ol[16];
+                tmem_ld16(tmem + lane_addr + 64 + c0, oh);
+                tmem_ld16(tmem + lane_addr + 96 + c0, ol);
                 tmem_wait_ld();
 #pragma unroll
-                for (int c = 0; c < 32; ++c) o[c] = __uint_as_float(orr[c]);
+                for (int i = 0; i < 16; ++i) o[i] = __uint_as_float(oh[i]) + __uint_as_float(ol[i]);
             } else {
 #pragma unroll
-                for (int c = 0; c < 32; ++c) o[c] = 0.f;
+                for (int i = 0; i < 16; ++i) o[i] = 0.f;
             }
             const int dim = 32 * qt + lane;
             if (p.splits == 1) {
-                int r = 0, g = 0;
+                int r = c0 / p.G, g = c0 % p.G;
 #pragma unroll
-                for (int c = 0; c < 32; ++c) {
-                    const float lc = __shfl_sync(0xffffffffu, lsum, c);
-                    if (c < R) {
+                for (int i = 0; i < 16; ++i) {
+                    const float l_i = __shfl_sync(0xffffffffu, lsum, i);
+                    if (c0 + i < R) {
                         T* dst = obase + (int64_t)(x.b * p.n_q + r) * p.o_srow +
                                  (int64_t)(x.kvh * p.G + g) * p.o_shead + dim;
-                        *dst = from_f32<T>(lc > 0.f ? o[c] / lc : 0.f);
+                        *dst = from_f32<T>(l_i > 0.f ? o[i] / l_i : 0.f);
                     }
                     if (++g == p.G) {
                         g = 0;
@@ -435,37 +510,77 @@ __global__ void __launch_bounds__(THREADS, 1)
             float* po = p.part_o + slot * R * D;
             float* pml = p.part_ml + slot * R * 2;
 #pragma unroll
-            for (int c = 0; c < 32; ++c)
-                if (c < R) __stcg(po + c * D + dim, o[c]);
-            if (st < 32 && lane < R) __stcg(reinterpret_cast<float2*>(pml + lane * 2), make_float2(mb, lsum));
-            __threadfence();
-            named_barrier_sync(2, 128);
-            if (st == 0) last_flag = atomicAdd(p.counters + pair, 1) == p.splits - 1;
-            named_barrier_sync(2, 128);
+            for (int i = 0; i < 16; ++i)
+                if (c0 + i < R) __stcg(po + (c0 + i) * D + dim, o[i]);
+            if (qt == 0 && lane < 16 && c0 + lane < R)
+                __stcg(reinterpret_cast<float2*>(pml + (c0 + lane) * 2), make_float2(mb_own, lsum));
+            // all partials of this CTA written -> one thread publishes them (fence + counter)
+            named_barrier_sync(2, SOFTMAX_THREADS);
+            if (st == 0) {
+                __threadfence();
+                const bool last = atomicAdd(p.counters + pair, 1) == p.splits - 1;
+                if (last) __threadfence();
+                last_flag = last;
+            }
+            named_barrier_sync(2, SOFTMAX_THREADS);
             if (!last_flag) continue;
-            __threadfence();
-            // last CTA of this (sequence, kv head): LSE-merge the splits, one dim per thread
+            // last CTA of this (sequence, kv head): LSE-merge the splits.
+            // (a) one thread per row: per-split weights exp2(m_s - M) / L into shared memory
             const float* ml = p.part_ml + (int64_t)pair * p.splits * R * 2;
             const float* pob = p.part_o + (int64_t)pair * p.splits * R * D;
-            int r = 0, g = 0;
-            for (int c = 0; c < R; ++c) {
+            float* W = reinterpret_cast<float*>(smem + OFF_W);  // [splits][32]
+            if (st < R) {
+                float mv[kMaxUmmaSplits], lv[kMaxUmmaSplits];
                 float Mx = NEG_INF;
-                for (int s2 = 0; s2 < p.splits; ++s2) Mx = fmaxf(Mx, __ldcg(ml + (s2 * R + c) * 2));
-                const float Bm = Mx == NEG_INF ? 0.f : Mx;
-                float Ls = 0.f, acc = 0.f;
-                for (int s2 = 0; s2 < p.splits; ++s2) {
-                    const float w = ex2(__ldcg(ml + (s2 * R + c) * 2) - Bm);
-                    Ls += w * __ldcg(ml + (s2 * R + c) * 2 + 1);
-                    acc += w * __ldcg(pob + ((int64_t)s2 * R + c) * D + dim);
+#pragma unroll
+                for (int s2 = 0; s2 < kMaxUmmaSplits; ++s2) {
+                    if (s2 < p.splits) {
+                        const float2 v = __ldcg(reinterpret_cast<const float2*>(ml + (s2 * R + st) * 2));
+                        mv[s2] = v.x;
+                        lv[s2] = v.y;
+                        Mx = fmaxf(Mx, v.x);
+                    }
                 }
-                T* dst = obase + (int64_t)(x.b * p.n_q + r) * p.o_srow + (int64_t)(x.kvh * p.G + g) * p.o_shead + dim;
-                *dst = from_f32<T>(Ls > 0.f ? acc / Ls : 0.f);
-                if (++g == p.G) {
-                    g = 0;
-                    ++r;
+                const float Bm = Mx == NEG_INF ? 0.f : Mx;
+                float Ls = 0.f;
+#pragma unroll
+                for (int s2 = 0; s2 < kMaxUmmaSplits; ++s2)
+                    if (s2 < p.splits) {
+                        mv[s2] = ex2(mv[s2] - Bm);
+                        Ls += mv[s2] * lv[s2];
+                    }
+                const float inv = Ls > 0.f ? 1.f / Ls : 0.f;
+#pragma unroll
+                for (int s2 = 0; s2 < kMaxUmmaSplits; ++s2)
+                    if (s2 < p.splits) W[s2 * 32 + st] = mv[s2] * inv;
+            }
+            named_barrier_sync(2, SOFTMAX_THREADS);
+            // (b) one dim and 16 rows per thread: independent loads of every split's partial
+            {
+                float acc[16];
+#pragma unroll
+                for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+                for (int s2 = 0; s2 < p.splits; ++s2) {
+#pragma unroll
+                    for (int i = 0; i < 16; ++i)
+                        if (c0 + i < R)
+                            acc[i] += W[s2 * 32 + c0 + i] * __ldcg(pob + ((int64_t)s2 * R + c0 + i) * D + dim);
+                }
+                int r = c0 / p.G, g = c0 % p.G;
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                    if (c0 + i < R) {
+                        T* dst = obase + (int64_t)(x.b * p.n_q + r) * p.o_srow +
+                                 (int64_t)(x.kvh * p.G + g) * p.o_shead + dim;
+                        *dst = from_f32<T>(acc[i]);
+                    }
+                    if (++g == p.G) {
+                        g = 0;
+                        ++r;
+                    }
                 }
             }
-            named_barrier_sync(2, 128);
+            named_barrier_sync(2, SOFTMAX_THREADS);
             if (st == 0) p.counters[pair] = 0;
         }
         if (!ok && lane == 0) atomicOr(p.err, SDB_KERR_TIMEOUT);

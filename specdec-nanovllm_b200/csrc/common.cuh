@@ -105,6 +105,20 @@ SDB_DEV void named_barrier_sync(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
+// Named barrier over `nthreads` threads that also ORs a predicate across them.
+SDB_DEV bool barrier_or(int id, int nthreads, bool pred) {
+    uint32_t out;
+    asm volatile(
+        "{\n\t.reg .pred pi, po;\n\t"
+        "setp.ne.u32 pi, %1, 0;\n\t"
+        "bar.red.or.pred po, %2, %3, pi;\n\t"
+        "selp.u32 %0, 1, 0, po;\n\t}"
+        : "=r"(out)
+        : "r"((uint32_t)pred), "r"(id), "r"(nthreads)
+        : "memory");
+    return out != 0;
+}
+
 SDB_DEV void ldsm_x4(uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3, uint32_t addr) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
                  : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
@@ -140,6 +154,14 @@ struct Half16<__nv_bfloat16> {
         const float2 f = __bfloat1622float2(h);
         return pack(lo - f.x, hi - f.y);
     }
+    // x = hi + lo with both 16-bit: hi is x truncated to bf16 (bit mask), x - hi is
+    // exact in f32 and is rounded once, so hi + lo carries ~16 significant bits of x.
+    static SDB_DEV void split(float x, uint16_t& hi, uint16_t& lo) {
+        const uint32_t b = __float_as_uint(x);
+        hi = (uint16_t)(b >> 16);
+        const float r = x - __uint_as_float(b & 0xffff0000u);
+        lo = __bfloat16_as_ushort(__float2bfloat16_rn(r));
+    }
     static constexpr CUtensorMapDataType tmap_type = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
 };
 
@@ -160,6 +182,11 @@ struct Half16<__half> {
         __half2 h = *reinterpret_cast<__half2*>(&head);
         const float2 f = __half22float2(h);
         return pack(lo - f.x, hi - f.y);
+    }
+    static SDB_DEV void split(float x, uint16_t& hi, uint16_t& lo) {
+        const __half h = __float2half_rn(x);
+        hi = __half_as_ushort(h);
+        lo = __half_as_ushort(__float2half_rn(x - __half2float(h)));
     }
     static constexpr CUtensorMapDataType tmap_type = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
 };
