@@ -8,25 +8,27 @@
 //
 // Formulation (transposed, so the 128-row tensor-core tile is the key axis):
 //   S^T[key, row] = K[key, :] . Q[row, :]        M = 128 keys, N = 32 rows, K = 128 dims
-//   O^T[dim, row] += V^T[dim, key] . P^T[key, row] M = 128 dims, N = 32 rows, K = 128 keys
+//   O^T[dim, row] += V^T[dim, key] . P[key, row]  M = 128 dims, N = 64, K = 128 keys
 // Both accumulators live in tensor memory (TMEM): S^T double-buffered in
-// columns [0, 64), O^T head / residual parts in [64, 96) / [96, 128).  K and V tiles arrive by TMA in the
-// 128-byte-swizzled layout the MMA descriptors read directly (K as a K-major A
-// operand, V as an MN-major A operand); Q^T and P^T are written by the softmax
-// warps as K-major B operands.  P is split into a 16-bit head and a 16-bit
-// residual and both multiply V, so the probabilities keep ~16 significant bits.
+// columns [0, 64), O^T head / residual parts in [64, 96) / [96, 128).  K, V and Q
+// arrive by TMA in the 128-byte-swizzled layout the MMA descriptors read directly
+// (K as a K-major A operand, V as an MN-major A operand, Q^T as a K-major B
+// operand); P is written by the softmax warps key-major (an MN-major B operand).
+// P is split into a 16-bit head and a 16-bit residual and both multiply V, so the
+// probabilities keep ~16 significant bits.
 //
 // Warp roles (320 threads, one CTA per SM, persistent over work items):
-//   warp 0      TMA producer: K/V tiles of 128 keys into a 3-stage ring
+//   warp 0      TMA producer: Q of each item, K/V tiles of 128 keys into a 3-stage ring
 //   warp 1      TMEM owner and MMA issuer (one thread)
 //   warps 2..9  softmax: thread = one TMEM lane (a key of S^T, a dim of O^T) and
 //               16 of the 32 columns (rows); column max / sum by an in-warp
 //               transpose reduction + a 4-warp exchange; lazy rescale (O is
 //               rescaled only when a row max grows by more than 2^8, exact
 //               because the reference point is kept).
-// Work items (split, kv head, sequence) are strided over the persistent CTAs;
-// the producer streams the next item's tiles while the current one finishes.
-// Every wait is bounded and reports SDB_KERR_TIMEOUT instead of hanging.
+// Work items (split, kv head, sequence) are strided over the persistent CTAs; the
+// producer streams the next item's tiles while the current one finishes.  With several splits per sequence, pa_umma_merge_kernel
+// LSE-merges the partials.  Every wait is bounded and reports SDB_KERR_TIMEOUT
+// instead of hanging.
 #include <cfloat>
 
 #include "attention_common.cuh"
@@ -43,30 +45,30 @@ constexpr int USTAGE = 2 * UTILE;         // K + V: 64 KB
 constexpr int UNS = 3;                    // stages
 constexpr int NROW = 32;                  // MMA N: query rows per (sequence, kv head)
 constexpr int QHALF = NROW * 128;         // 4 KB
-// P^T of tile t is written into the K half of tile t's stage once S(t) has read K,
-// as one N = 64 B operand: rows 0..31 are the 16-bit heads of P^T's 32 columns,
-// rows 32..63 their residuals, so a single MMA per key step reads V once and
-// accumulates O_head and O_residual side by side (64 TMEM columns).  Two key halves
-// of 64 rows x 128 B.  The stage ring thus multi-buffers P and the P.V completion
-// that frees the stage also frees P.
+// P of tile t is written into the first K half of tile t's stage once S(t) has read
+// K, as one N = 64 B operand: 128 key rows of 128 B, columns 0..31 the 16-bit heads
+// of the 32 rows' probabilities, columns 32..63 their residuals, so a single MMA per
+// key step reads V once and accumulates O_head and O_residual side by side (64 TMEM
+// columns).  The stage ring thus multi-buffers P and the P.V completion that frees
+// the stage also frees P.
 constexpr int PROWS = 2 * NROW;
-constexpr int PKHALF = PROWS * 128;       // 8 KB
 constexpr int QBUF = 2 * QHALF;           // one item's Q^T (8 KB)
 constexpr int OFF_Q = UNS * USTAGE;       // two Q^T buffers: item i uses buffer i & 1
 constexpr int OFF_RED = OFF_Q + 2 * QBUF;             // red_max[4][32], red_sum[4][32]
 constexpr int kMaxUmmaSplits = 16;
 constexpr int OFF_W = OFF_RED + 2 * 4 * 32 * 4;       // merge weights [splits][32] + 1/L [32]
 constexpr int OFF_BAR = OFF_W + (kMaxUmmaSplits + 1) * 32 * 4;
-// barriers: full[3] empty[3] s_full[2] s_free[2] p_full q_ready[2] fin
-constexpr int NBAR = UNS * 2 + 2 + 2 + 4;
+// barriers: full[3] empty[3] s_full[2] s_free[2] p_full q_ready[2] q_free[2] fin
+constexpr int NBAR = UNS * 2 + 2 + 2 + 1 + 2 + 2 + 1;
 constexpr int OFF_TMEM = OFF_BAR + NBAR * 8;
 constexpr int SMEM_BYTES = OFF_TMEM + 16 + 1024;  // + alignment slack
 constexpr uint32_t TMEM_COLS = 128;
 constexpr int SOFTMAX_THREADS = 256;  // 8 warps
+constexpr int SOFTMAX_WARPS = SOFTMAX_THREADS / 32;  // one mbarrier arrival per warp
 constexpr int THREADS = 64 + SOFTMAX_THREADS;
 
 struct Bars {
-    uint32_t full0, empty0, sfull0, sfree0, pfull, qready0, fin;
+    uint32_t full0, empty0, sfull0, sfree0, pfull, qready0, qfree0, fin;
 };
 
 SDB_DEV Bars bars_at(uint32_t base) {
@@ -77,7 +79,8 @@ SDB_DEV Bars bars_at(uint32_t base) {
     b.sfree0 = b.sfull0 + 16;
     b.pfull = b.sfree0 + 16;
     b.qready0 = b.pfull + 8;
-    b.fin = b.qready0 + 16;
+    b.qfree0 = b.qready0 + 16;
+    b.fin = b.qfree0 + 16;
     return b;
 }
 
@@ -97,6 +100,26 @@ SDB_DEV Item item_at(const Params& p, int it) {
     x.ntiles = x.k1 > x.k0 ? (x.k1 - x.k0 + UBN - 1) / UBN : 0;
     return x;
 }
+
+// Position (item, tile) in the sequence of tiles a persistent CTA processes: items
+// blockIdx.x, blockIdx.x + gridDim.x, ... and the tiles of each in order (items without
+// tiles are skipped).  it == total_items once the sequence is exhausted.
+struct TileCursor {
+    int it, t;
+    Item x;
+    SDB_DEV TileCursor(const Params& p, int first, int total_items) : it(first), t(-1) {
+        if (it < total_items) x = item_at(p, it);
+        advance(p, total_items);
+    }
+    SDB_DEV void advance(const Params& p, int total_items) {
+        ++t;
+        while (it < total_items && t >= x.ntiles) {
+            it += gridDim.x;
+            t = 0;
+            if (it < total_items) x = item_at(p, it);
+        }
+    }
+};
 
 // Wait that becomes a no-op once this thread has seen a timeout: the softmax warps
 // keep executing the same sequence of named barriers after a failure (never
@@ -126,41 +149,10 @@ SDB_DEV float transpose_reduce16(float (&v)[16], int lane) {
     return MAX ? fmaxf(v[0], other) : v[0] + other;
 }
 
-// Q^T of item `it` into Q buffer `buf` as a K-major swizzled B operand (rows >= R zero),
-// then release it to the MMA warp.  Called by the 256 softmax threads.
-template <typename T>
-SDB_DEV void write_q(const Params& p, uint8_t* smem, int it, int buf, int st, const Bars& bar) {
-    const Item x = item_at(p, it);
-    const T* qbase = reinterpret_cast<const T*>(p.q);
-#pragma unroll
-    for (int i = 0; i < 2; ++i) {
-        const int u = st + SOFTMAX_THREADS * i;
-        const int c = u >> 4, chk = u & 15;
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (c < p.R) {
-            const int r = c / p.G, g = c % p.G;
-            v = __ldg(reinterpret_cast<const uint4*>(qbase + (int64_t)(x.b * p.n_q + r) * p.q_srow +
-                                                     (int64_t)(x.kvh * p.G + g) * p.q_shead + chk * 8));
-        }
-        *reinterpret_cast<uint4*>(smem + OFF_Q + buf * QBUF + (chk >> 3) * QHALF + c * 128 +
-                                  (((chk & 7) ^ (c & 7)) << 4)) = v;
-    }
-    fence_proxy_async_smem();
-    tc_fence_before();
-    mbar_arrive(bar.qready0 + 8 * buf);
-}
-
-// Next work item of this CTA after `it` that has at least one tile (or total_items).
-SDB_DEV int next_busy_item(const Params& p, int it, int total_items) {
-    for (it += gridDim.x; it < total_items; it += gridDim.x)
-        if (item_at(p, it).ntiles > 0) return it;
-    return total_items;
-}
-
 template <typename T>
 __global__ void __launch_bounds__(THREADS, 1)
     pa_umma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
-                   const Params p, int total_items) {
+                   const __grid_constant__ CUtensorMap qmap, const Params p, int total_items) {
     using H = Half16<T>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -170,7 +162,6 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_TMEM);
     float* red_max = reinterpret_cast<float*>(smem + OFF_RED);
     float* red_sum = red_max + 4 * 32;
-    __shared__ int last_flag;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     if (threadIdx.x == 0) {
@@ -180,11 +171,13 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(bar.sfull0 + 8 * i, 1);
-            mbar_init(bar.sfree0 + 8 * i, SOFTMAX_THREADS);
+            mbar_init(bar.sfree0 + 8 * i, SOFTMAX_WARPS);
         }
-        mbar_init(bar.pfull, SOFTMAX_THREADS);
-        mbar_init(bar.qready0, SOFTMAX_THREADS);
-        mbar_init(bar.qready0 + 8, SOFTMAX_THREADS);
+        mbar_init(bar.pfull, SOFTMAX_WARPS);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(bar.qready0 + 8 * i, 1);
+            mbar_init(bar.qfree0 + 8 * i, 1);
+        }
         mbar_init(bar.fin, 1);
         fence_mbarrier_init();
     }
@@ -192,6 +185,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
         tmem_relinquish();
     }
+    // Q buffers: TMA writes rows 0..R-1 of each; rows R..31 (pad columns of S^T) stay zero
+    for (int i = threadIdx.x; i < 2 * QBUF / 16; i += THREADS)
+        reinterpret_cast<uint4*>(smem + OFF_Q)[i] = make_uint4(0, 0, 0, 0);
+    fence_proxy_async_smem();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -202,38 +199,60 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (lane == 0) {
             prefetch_tensormap(&kmap);
             prefetch_tensormap(&vmap);
+            prefetch_tensormap(&qmap);
             const uint64_t pol = l2_policy_evict_first();
-            int gt = 0;
+            const uint64_t qpol = l2_policy_evict_normal();  // every split of a sequence reads Q
+            int gt = 0, nq = 0;
             bool ok = true;
-            for (int it = blockIdx.x; it < total_items && ok; it += gridDim.x) {
-                const Item x = item_at(p, it);
-                const int* btrow = p.bt + (int64_t)x.b * p.bt_stride;
-                for (int t = 0; t < x.ntiles; ++t, ++gt) {
-                    const int s = gt % UNS;
-                    if (gt >= UNS && !mbar_wait(bar.empty0 + 8 * s, ((gt / UNS) - 1) & 1)) {
-                        atomicOr(p.err, SDB_KERR_TIMEOUT);
+            TileCursor ld(p, blockIdx.x, total_items);
+            while (ld.it < total_items) {
+                const int j = ld.x.k0 + ld.t * UBN;
+                // the block id is read before the waits, off the stage-hold path
+                int blk = p.bt[(int64_t)ld.x.b * p.bt_stride + j / p.page];
+                if (ld.t == 0) {
+                    // Q^T rows (r, g) -> row r*G + g of Q buffer nq & 1, K-major 128-byte swizzle;
+                    // the buffer is free once the S MMAs of the item two before have completed
+                    const int qb = nq & 1;
+                    if (nq >= 2 && !mbar_wait(bar.qfree0 + 8 * qb, ((nq >> 1) - 1) & 1)) {
                         ok = false;
                         break;
                     }
-                    const int j = x.k0 + t * UBN;
-                    int blk = btrow[j / p.page];
-                    if (blk < 0 || blk >= p.num_blocks) {
-                        atomicOr(p.err, SDB_KERR_BLOCK_ID);
-                        blk = 0;
-                    }
-                    const int off = j % p.page;
-                    const uint32_t kdst = sbase + s * USTAGE;
-                    const uint32_t vdst = kdst + UTILE;
-                    const uint32_t fb = bar.full0 + 8 * s;
-                    mbar_arrive_expect_tx(fb, USTAGE);
-                    tma_load_4d(kdst, &kmap, fb, 0, x.kvh, off, blk, pol);
-                    tma_load_4d(kdst + UHALF, &kmap, fb, 64, x.kvh, off, blk, pol);
-                    tma_load_4d(vdst, &vmap, fb, 0, x.kvh, off, blk, pol);
-                    tma_load_4d(vdst + UHALF, &vmap, fb, 64, x.kvh, off, blk, pol);
+                    const uint32_t qdst = sbase + OFF_Q + qb * QBUF;
+                    mbar_arrive_expect_tx(bar.qready0 + 8 * qb, 2 * 128 * p.R);
+                    tma_load_4d(qdst, &qmap, bar.qready0 + 8 * qb, 0, 0, ld.x.kvh, ld.x.b * p.n_q, qpol);
+                    tma_load_4d(qdst + QHALF, &qmap, bar.qready0 + 8 * qb, 64, 0, ld.x.kvh, ld.x.b * p.n_q, qpol);
+                    ++nq;
                 }
+                const int s = gt % UNS;
+                if (gt >= UNS && !mbar_wait(bar.empty0 + 8 * s, ((gt / UNS) - 1) & 1)) {
+                    ok = false;
+                    break;
+                }
+                if (blk < 0 || blk >= p.num_blocks) {
+                    atomicOr(p.err, SDB_KERR_BLOCK_ID);
+                    blk = 0;
+                }
+                const int off = j % p.page;
+                const uint32_t kdst = sbase + s * USTAGE;
+                const uint32_t vdst = kdst + UTILE;
+                const uint32_t fb = bar.full0 + 8 * s;
+                mbar_arrive_expect_tx(fb, USTAGE);
+                tma_load_4d(kdst, &kmap, fb, 0, ld.x.kvh, off, blk, pol);
+                tma_load_4d(kdst + UHALF, &kmap, fb, 64, ld.x.kvh, off, blk, pol);
+                tma_load_4d(vdst, &vmap, fb, 0, ld.x.kvh, off, blk, pol);
+                tma_load_4d(vdst + UHALF, &vmap, fb, 64, ld.x.kvh, off, blk, pol);
+                ++gt;
+                ld.advance(p, total_items);
             }
+            if (!ok) atomicOr(p.err, SDB_KERR_TIMEOUT);
             for (int g = gt - UNS > 0 ? gt - UNS : 0; g < gt; ++g) {  // drain own copies
                 if (!mbar_wait(bar.full0 + 8 * (g % UNS), (g / UNS) & 1)) {
+                    atomicOr(p.err, SDB_KERR_TIMEOUT);
+                    break;
+                }
+            }
+            for (int n = nq - 2 > 0 ? nq - 2 : 0; n < nq; ++n) {
+                if (!mbar_wait(bar.qready0 + 8 * (n & 1), (n >> 1) & 1)) {
                     atomicOr(p.err, SDB_KERR_TIMEOUT);
                     break;
                 }
@@ -244,10 +263,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (lane == 0) {
             constexpr bool BF = std::is_same<T, __nv_bfloat16>::value;
             constexpr uint32_t IDESC_S = idesc_f16(BF, false, false, 128, NROW);
-            constexpr uint32_t IDESC_PV = idesc_f16(BF, true, false, 128, PROWS);
+            constexpr uint32_t IDESC_PV = idesc_f16(BF, true, true, 128, PROWS);
             int gt = 0, nitem = 0;
             bool ok = true;
-            // O^T += V(g)^T . P^T(g), head then residual; completion frees stage g (K, V and P)
+            // O^T += V(g)^T . P(g), heads and residuals as N = 64; completion frees stage g (K, V and P)
             auto pv = [&](int g, bool first) -> bool {
                 if (!mbar_wait(bar.pfull, g & 1)) return false;
                 tc_fence_after();
@@ -256,7 +275,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                 for (int ks = 0; ks < 8; ++ks) {
                     const uint64_t a = sdesc_sw128(vbase + ks * 2048, UHALF, 1024);
-                    const uint64_t b = sdesc_sw128(stage + (ks >> 2) * PKHALF + (ks & 3) * 32, 16, 1024);
+                    const uint64_t b = sdesc_sw128(stage + ks * 2048, UHALF, 1024);
                     umma_f16_ss(tmem + 64, a, b, IDESC_PV, (first && ks == 0) ? 0u : 1u);
                 }
                 umma_commit(bar.empty0 + 8 * (g % UNS));
@@ -288,6 +307,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                         umma_f16_ss(tmem + sb * 32, a, b, IDESC_S, ks > 0 ? 1u : 0u);
                     }
                     umma_commit(bar.sfull0 + 8 * sb);
+                    if (t == x.ntiles - 1) umma_commit(bar.qfree0 + 8 * (nitem & 1));  // Q buffer read
                     if (t >= 1 && !pv(gt - 1, t == 1)) {
                         ok = false;
                         break;
@@ -313,7 +333,6 @@ __global__ void __launch_bounds__(THREADS, 1)
         // (first tile of an item, or a row max that grew) all warps take the exact path:
         // column max over the 128 keys, new reference = max, partial sums and O rescaled.
         const int sw = warp - 2;            // 0..7
-        const int st = threadIdx.x - 64;    // 0..255
         const int qt = warp & 3;
         const int ch = sw >> 2;
         const int c0 = 16 * ch;             // first column (row) of this thread
@@ -324,22 +343,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         int gt = 0;
         bool ok = true;
         T* obase = reinterpret_cast<T*>(p.out);
-        // Q^T buffers: the i-th item with tiles uses buffer i & 1; the next one is written
-        // while the current one runs, so the MMA warp starts an item without waiting.
-        int qi = 0;
-        {
-            const int first = item_at(p, blockIdx.x < total_items ? blockIdx.x : 0).ntiles > 0
-                                  ? blockIdx.x
-                                  : next_busy_item(p, blockIdx.x, total_items);
-            if (blockIdx.x < total_items && first < total_items) write_q<T>(p, smem, first, 0, st, bar);
-        }
         for (int it = blockIdx.x; it < total_items; it += gridDim.x) {
             const Item x = item_at(p, it);
-            if (x.ntiles > 0) {
-                const int nxt = next_busy_item(p, it, total_items);
-                if (nxt < total_items) write_q<T>(p, smem, nxt, (qi + 1) & 1, st, bar);
-                ++qi;
-            }
 
             float mb_own = NEG_INF;   // reference of column c0 + lc
             float mbv[16], lpart[16];
@@ -358,7 +363,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                 tmem_ld16(tmem + lane_addr + sb * 32 + c0, sr);
                 tmem_wait_ld();
                 tc_fence_before();
-                mbar_arrive(bar.sfree0 + 8 * sb);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar.sfree0 + 8 * sb);
 
                 const int key = j0 + 32 * qt + lane;
                 float xv[16];
@@ -439,25 +445,24 @@ __global__ void __launch_bounds__(THREADS, 1)
                             *reinterpret_cast<uint4*>(vrow + q16 * 16) = make_uint4(0, 0, 0, 0);
                     }
                 }
-                // P^T (heads in rows 0..31, residuals in rows 32..63) into the K half of this
-                // stage (S(t) has read K); row r of a key half sits at r*128, chunk ^ (r & 7)
+                // P into the first K half of this stage (S(t) has read K): row `key` holds
+                // 64 columns, heads of rows 0..31 then their residuals, 128-byte swizzle
+                // (16-byte chunk j of row k at j ^ (k & 7)): the MN-major B operand of P.V
                 {
-                    const int half = kin >> 6, kk = kin & 63;
-                    const int chunk = kk >> 3, byte = (kk & 7) * 2;
-                    uint8_t* pb = stage + half * PKHALF + byte;
+                    uint32_t hw[8], lw[8];
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        const int c = c0 + i;
-                        uint16_t hi, lo;
-                        H::split(pv[i], hi, lo);
-                        const int o = c * 128 + ((chunk ^ (c & 7)) << 4);
-                        *reinterpret_cast<uint16_t*>(pb + o) = hi;
-                        *reinterpret_cast<uint16_t*>(pb + o + NROW * 128) = lo;  // row c + 32: same swizzle
-                    }
+                    for (int i = 0; i < 8; ++i) H::split2(pv[2 * i], pv[2 * i + 1], hw[i], lw[i]);
+                    uint8_t* prow = stage + kin * 128;
+                    const int sw = kin & 7;
+                    *reinterpret_cast<uint4*>(prow + (((2 * ch) ^ sw) << 4)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+                    *reinterpret_cast<uint4*>(prow + (((2 * ch + 1) ^ sw) << 4)) = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+                    *reinterpret_cast<uint4*>(prow + (((4 + 2 * ch) ^ sw) << 4)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+                    *reinterpret_cast<uint4*>(prow + (((5 + 2 * ch) ^ sw) << 4)) = make_uint4(lw[4], lw[5], lw[6], lw[7]);
                 }
                 fence_proxy_async_smem();
                 tc_fence_before();
-                mbar_arrive(bar.pfull);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar.pfull);
             }
 
             // ---- item epilogue: row sums, then O^T column c is row c (this thread: dim 32*qt + lane)
@@ -514,74 +519,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 if (c0 + i < R) __stcg(po + (c0 + i) * D + dim, o[i]);
             if (qt == 0 && lane < 16 && c0 + lane < R)
                 __stcg(reinterpret_cast<float2*>(pml + (c0 + lane) * 2), make_float2(mb_own, lsum));
-            // all partials of this CTA written -> one thread publishes them (fence + counter)
-            named_barrier_sync(2, SOFTMAX_THREADS);
-            if (st == 0) {
-                __threadfence();
-                const bool last = atomicAdd(p.counters + pair, 1) == p.splits - 1;
-                if (last) __threadfence();
-                last_flag = last;
-            }
-            named_barrier_sync(2, SOFTMAX_THREADS);
-            if (!last_flag) continue;
-            // last CTA of this (sequence, kv head): LSE-merge the splits.
-            // (a) one thread per row: per-split weights exp2(m_s - M) / L into shared memory
-            const float* ml = p.part_ml + (int64_t)pair * p.splits * R * 2;
-            const float* pob = p.part_o + (int64_t)pair * p.splits * R * D;
-            float* W = reinterpret_cast<float*>(smem + OFF_W);  // [splits][32]
-            if (st < R) {
-                float mv[kMaxUmmaSplits], lv[kMaxUmmaSplits];
-                float Mx = NEG_INF;
-#pragma unroll
-                for (int s2 = 0; s2 < kMaxUmmaSplits; ++s2) {
-                    if (s2 < p.splits) {
-                        const float2 v = __ldcg(reinterpret_cast<const float2*>(ml + (s2 * R + st) * 2));
-                        mv[s2] = v.x;
-                        lv[s2] = v.y;
-                        Mx = fmaxf(Mx, v.x);
-                    }
-                }
-                const float Bm = Mx == NEG_INF ? 0.f : Mx;
-                float Ls = 0.f;
-#pragma unroll
-                for (int s2 = 0; s2 < kMaxUmmaSplits; ++s2)
-                    if (s2 < p.splits) {
-                        mv[s2] = ex2(mv[s2] - Bm);
-                        Ls += mv[s2] * lv[s2];
-                    }
-                const float inv = Ls > 0.f ? 1.f / Ls : 0.f;
-#pragma unroll
-                for (int s2 = 0; s2 < kMaxUmmaSplits; ++s2)
-                    if (s2 < p.splits) W[s2 * 32 + st] = mv[s2] * inv;
-            }
-            named_barrier_sync(2, SOFTMAX_THREADS);
-            // (b) one dim and 16 rows per thread: independent loads of every split's partial
-            {
-                float acc[16];
-#pragma unroll
-                for (int i = 0; i < 16; ++i) acc[i] = 0.f;
-                for (int s2 = 0; s2 < p.splits; ++s2) {
-#pragma unroll
-                    for (int i = 0; i < 16; ++i)
-                        if (c0 + i < R)
-                            acc[i] += W[s2 * 32 + c0 + i] * __ldcg(pob + ((int64_t)s2 * R + c0 + i) * D + dim);
-                }
-                int r = c0 / p.G, g = c0 % p.G;
-#pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    if (c0 + i < R) {
-                        T* dst = obase + (int64_t)(x.b * p.n_q + r) * p.o_srow +
-                                 (int64_t)(x.kvh * p.G + g) * p.o_shead + dim;
-                        *dst = from_f32<T>(acc[i]);
-                    }
-                    if (++g == p.G) {
-                        g = 0;
-                        ++r;
-                    }
-                }
-            }
-            named_barrier_sync(2, SOFTMAX_THREADS);
-            if (st == 0) p.counters[pair] = 0;
+            // the LSE merge of the splits runs as a separate kernel (pa_umma_merge_kernel)
         }
         if (!ok && lane == 0) atomicOr(p.err, SDB_KERR_TIMEOUT);
     }
@@ -590,6 +528,65 @@ __global__ void __launch_bounds__(THREADS, 1)
     __syncthreads();
     tc_fence_after();
     if (warp == 1) tmem_dealloc(tmem, TMEM_COLS);
+}
+
+// LSE merge of the split partials: one CTA per (sequence, kv head), one thread per
+// dim; per-split weights exp2(m_s - M) / L computed once per row into shared memory.
+template <typename T>
+__global__ void __launch_bounds__(128) pa_umma_merge_kernel(const Params p) {
+    __shared__ float W[kMaxUmmaSplits][NROW];
+    const int pair = blockIdx.x;
+    const int b = pair / p.Hkv, kvh = pair % p.Hkv;
+    const int R = p.R;
+    const float* ml = p.part_ml + (int64_t)pair * p.splits * R * 2;
+    const float* pob = p.part_o + (int64_t)pair * p.splits * R * D;
+    const int t = threadIdx.x;
+    if (t < R) {
+        float mv[kMaxUmmaSplits], lv[kMaxUmmaSplits];
+        float Mx = NEG_INF;
+#pragma unroll
+        for (int s2 = 0; s2 < kMaxUmmaSplits; ++s2)
+            if (s2 < p.splits) {
+                const float2 v = *reinterpret_cast<const float2*>(ml + (s2 * R + t) * 2);
+                mv[s2] = v.x;
+                lv[s2] = v.y;
+                Mx = fmaxf(Mx, v.x);
+            }
+        const float Bm = Mx == NEG_INF ? 0.f : Mx;
+        float Ls = 0.f;
+#pragma unroll
+        for (int s2 = 0; s2 < kMaxUmmaSplits; ++s2)
+            if (s2 < p.splits) {
+                mv[s2] = ex2(mv[s2] - Bm);
+                Ls += mv[s2] * lv[s2];
+            }
+        const float inv = Ls > 0.f ? 1.f / Ls : 0.f;
+#pragma unroll
+        for (int s2 = 0; s2 < kMaxUmmaSplits; ++s2)
+            if (s2 < p.splits) W[s2][t] = mv[s2] * inv;
+    }
+    __syncthreads();
+    T* obase = reinterpret_cast<T*>(p.out);
+    int r = 0, g = 0;
+    for (int c0 = 0; c0 < R; c0 += 8) {
+        float acc[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+        for (int s2 = 0; s2 < p.splits; ++s2)
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                if (c0 + i < R) acc[i] += W[s2][c0 + i] * pob[((int64_t)s2 * R + c0 + i) * D + t];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            if (c0 + i < R)
+                obase[(int64_t)(b * p.n_q + r) * p.o_srow + (int64_t)(kvh * p.G + g) * p.o_shead + t] =
+                    from_f32<T>(acc[i]);
+            if (++g == p.G) {
+                g = 0;
+                ++r;
+            }
+        }
+    }
 }
 
 }  // namespace umma
@@ -653,20 +650,33 @@ int launch_umma(const void* k_cache, const void* v_cache, int dtype, int64_t sb,
     if (rc) return rc;
     rc = encode_tensor_map(&vm, dt, 4, const_cast<void*>(v_cache), dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
+    // Q viewed as (dim, head in group, kv head, query row): one box is the R = n_q * G rows
+    // of one (sequence, kv head) in row order r * G + g, 64 dims each
+    const int G = p.G;
+    cuuint64_t qdims[4] = {(cuuint64_t)D, (cuuint64_t)G, (cuuint64_t)p.Hkv, (cuuint64_t)p.B * p.n_q};
+    cuuint64_t qstrides[3] = {(cuuint64_t)p.q_shead * 2, (cuuint64_t)p.q_shead * G * 2, (cuuint64_t)p.q_srow * 2};
+    cuuint32_t qbox[4] = {64, (cuuint32_t)G, 1, (cuuint32_t)p.n_q};
+    CUtensorMap qm;
+    rc = encode_tensor_map(&qm, dt, 4, const_cast<void*>(p.q), qdims, qstrides, qbox, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
     const int total_items = p.B * p.Hkv * splits;
     const int grid = total_items < sms ? total_items : sms;
     if (dtype == SDB_BF16) {
         auto kern = umma::pa_umma_kernel<__nv_bfloat16>;
         rc = ensure_smem_attr(reinterpret_cast<const void*>(kern), umma::SMEM_BYTES, 40);
         if (rc) return rc;
-        kern<<<grid, umma::THREADS, umma::SMEM_BYTES, st>>>(km, vm, p, total_items);
+        kern<<<grid, umma::THREADS, umma::SMEM_BYTES, st>>>(km, vm, qm, p, total_items);
     } else {
         auto kern = umma::pa_umma_kernel<__half>;
         rc = ensure_smem_attr(reinterpret_cast<const void*>(kern), umma::SMEM_BYTES, 41);
         if (rc) return rc;
-        kern<<<grid, umma::THREADS, umma::SMEM_BYTES, st>>>(km, vm, p, total_items);
+        kern<<<grid, umma::THREADS, umma::SMEM_BYTES, st>>>(km, vm, qm, p, total_items);
     }
-    return cuda_status(cudaGetLastError(), "pa_umma_kernel launch");
+    rc = cuda_status(cudaGetLastError(), "pa_umma_kernel launch");
+    if (rc || splits == 1) return rc;
+    if (dtype == SDB_BF16) umma::pa_umma_merge_kernel<__nv_bfloat16><<<p.B * p.Hkv, 128, 0, st>>>(p);
+    else umma::pa_umma_merge_kernel<__half><<<p.B * p.Hkv, 128, 0, st>>>(p);
+    return cuda_status(cudaGetLastError(), "pa_umma_merge_kernel launch");
 }
 
 }  // namespace attn

@@ -97,6 +97,12 @@ SDB_DEV uint64_t l2_policy_evict_first() {
     return pol;
 }
 
+SDB_DEV uint64_t l2_policy_evict_normal() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
+}
+
 SDB_DEV void prefetch_tensormap(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -162,6 +168,12 @@ struct Half16<__nv_bfloat16> {
         const float r = x - __uint_as_float(b & 0xffff0000u);
         lo = __bfloat16_as_ushort(__float2bfloat16_rn(r));
     }
+    // split() of two columns at once: packed heads (x0 in the low half) and packed residuals.
+    static SDB_DEV void split2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+        const uint32_t b0 = __float_as_uint(x0), b1 = __float_as_uint(x1);
+        hi = __byte_perm(b0, b1, 0x7632);
+        lo = pack(x0 - __uint_as_float(b0 & 0xffff0000u), x1 - __uint_as_float(b1 & 0xffff0000u));
+    }
     static constexpr CUtensorMapDataType tmap_type = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
 };
 
@@ -187,6 +199,12 @@ struct Half16<__half> {
         const __half h = __float2half_rn(x);
         hi = __half_as_ushort(h);
         lo = __half_as_ushort(__float2half_rn(x - __half2float(h)));
+    }
+    static SDB_DEV void split2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+        const __half2 h = __floats2half2_rn(x0, x1);
+        const float2 f = __half22float2(h);
+        hi = *reinterpret_cast<const uint32_t*>(&h);
+        lo = pack(x0 - f.x, x1 - f.y);
     }
     static constexpr CUtensorMapDataType tmap_type = CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
 };
