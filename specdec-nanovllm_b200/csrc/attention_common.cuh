@@ -28,6 +28,10 @@ struct Params {
     unsigned* checksum;  // read-only twin only
     int B, n_q, G, R, Hkv, page, max_blocks, num_blocks, splits, chunk;
     float scale_log2;
+    // tcgen05 path, balanced partition: tile slots per sequence (0 = strided static
+    // splits instead), all sequences' slots, and the CTA groups (Hkv CTAs each) sharing them
+    int flat_T, flat_grid;
+    long long flat_total;
 };
 
 struct WsLayout {

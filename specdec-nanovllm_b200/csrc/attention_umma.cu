@@ -56,13 +56,14 @@ constexpr int QBUF = 2 * QHALF;           // one item's Q^T (8 KB)
 constexpr int OFF_Q = UNS * USTAGE;       // two Q^T buffers: item i uses buffer i & 1
 constexpr int OFF_RED = OFF_Q + 2 * QBUF;             // red_max[4][32], red_sum[4][32]
 constexpr int kMaxUmmaSplits = 16;
-constexpr int OFF_W = OFF_RED + 2 * 4 * 32 * 4;       // merge weights [splits][32] + 1/L [32]
-constexpr int OFF_BAR = OFF_W + (kMaxUmmaSplits + 1) * 32 * 4;
+constexpr int OFF_BAR = OFF_RED + 2 * 4 * 32 * 4;
 // barriers: full[3] empty[3] s_full[2] s_free[2] p_full q_ready[2] q_free[2] fin
 constexpr int NBAR = UNS * 2 + 2 + 2 + 1 + 2 + 2 + 1;
 constexpr int OFF_TMEM = OFF_BAR + NBAR * 8;
 constexpr int SMEM_BYTES = OFF_TMEM + 16 + 1024;  // + alignment slack
+// TMEM columns: S^T buffers [0, 64), O^T heads / residuals [64, 96) / [96, 128)
 constexpr uint32_t TMEM_COLS = 128;
+constexpr uint32_t TCOL_O = 64;
 constexpr int SOFTMAX_THREADS = 256;  // 8 warps
 constexpr int SOFTMAX_WARPS = SOFTMAX_THREADS / 32;  // one mbarrier arrival per warp
 constexpr int THREADS = 64 + SOFTMAX_THREADS;
@@ -84,39 +85,90 @@ SDB_DEV Bars bars_at(uint32_t base) {
     return b;
 }
 
+// A contiguous key range [k0, k1) of one (sequence b, kv head) pair processed by one
+// CTA.  `direct`: the CTA holds every key of the pair and writes the output itself;
+// otherwise it writes partial `slot` of the pair for pa_umma_merge_kernel.
 struct Item {
-    int b, kvh, split, L, k0, k1, ntiles;
+    int b, kvh, slot, L, k0, k1, ntiles, span;
+    bool direct;
 };
 
-SDB_DEV Item item_at(const Params& p, int it) {
+SDB_DEV Item make_item(const Params& p, int pair, int k0, int k1, int slot, bool direct, int span) {
     Item x;
-    x.split = it % p.splits;
-    const int rest = it / p.splits;
-    x.kvh = rest % p.Hkv;
-    x.b = rest / p.Hkv;
+    x.kvh = pair % p.Hkv;
+    x.b = pair / p.Hkv;
     x.L = load_len(p, x.b);
-    x.k0 = x.split * p.chunk;
-    x.k1 = min(x.k0 + p.chunk, x.L);
+    x.k0 = k0;
+    x.k1 = min(k1, x.L);
     x.ntiles = x.k1 > x.k0 ? (x.k1 - x.k0 + UBN - 1) / UBN : 0;
+    x.slot = slot;
+    x.direct = direct;
+    x.span = span;
     return x;
 }
 
-// Position (item, tile) in the sequence of tiles a persistent CTA processes: items
-// blockIdx.x, blockIdx.x + gridDim.x, ... and the tiles of each in order (items without
-// tiles are skipped).  it == total_items once the sequence is exhausted.
-struct TileCursor {
-    int it, t;
-    Item x;
-    SDB_DEV TileCursor(const Params& p, int first, int total_items) : it(first), t(-1) {
-        if (it < total_items) x = item_at(p, it);
-        advance(p, total_items);
+// Balanced partition in CTA groups: the CTAs form flat_grid groups of Hkv, CTA
+// g * Hkv + h taking kv head h.  The sequences' tile slots (flat_T per sequence) are
+// laid end to end and group g owns [start(g), start(g + 1)) with start(g) =
+// floor(g * total / flat_grid): every CTA streams the same number of tiles (+-1),
+// the Hkv heads of a sequence are read in lockstep by one group (the heads of a key
+// row share its DRAM pages), and a sequence is split only where a group boundary
+// falls inside it.
+SDB_DEV long long flat_start(const Params& p, int g) { return (long long)g * p.flat_total / p.flat_grid; }
+SDB_DEV int flat_group_of(const Params& p, long long f) {
+    int g = (int)(f * p.flat_grid / p.flat_total);
+    if (g + 1 < p.flat_grid && flat_start(p, g + 1) <= f) ++g;
+    return g;
+}
+
+// The items of this CTA in order: with the balanced partition, the pieces of its slot
+// range; otherwise (static splits) items blockIdx.x, blockIdx.x + gridDim.x, ... of
+// the (pair, split) list, split fastest.
+struct WorkIter {
+    int f, f1;  // the host keeps every flat index and item count below 2^31
+    SDB_DEV explicit WorkIter(const Params& p) {
+        if (p.flat_T > 0) {
+            const int g = blockIdx.x / p.Hkv;
+            f = (int)flat_start(p, g);
+            f1 = (int)flat_start(p, g + 1);
+        } else {
+            f = blockIdx.x;
+            f1 = p.B * p.Hkv * p.splits;
+        }
     }
-    SDB_DEV void advance(const Params& p, int total_items) {
+    SDB_DEV bool valid() const { return f < f1; }
+    SDB_DEV Item item(const Params& p) const {
+        if (p.flat_T > 0) {
+            const int b = f / p.flat_T, t0 = f % p.flat_T;
+            const int t1 = min(p.flat_T, t0 + (f1 - f));
+            const bool whole = t0 == 0 && t1 == p.flat_T;
+            const int g = blockIdx.x / p.Hkv;
+            const int slot = whole ? 0 : g - flat_group_of(p, (long long)b * p.flat_T);
+            return make_item(p, b * p.Hkv + (int)blockIdx.x % p.Hkv, t0 * UBN, t1 * UBN, slot, whole, t1 - t0);
+        }
+        const int it = f, split = it % p.splits;
+        return make_item(p, it / p.splits, split * p.chunk, split * p.chunk + p.chunk, split, p.splits == 1, 0);
+    }
+    SDB_DEV void next(const Params& p, const Item& x) { f += p.flat_T > 0 ? x.span : gridDim.x; }
+};
+
+// Position (item, tile) in the sequence of tiles this CTA processes (items without
+// tiles are skipped); valid() is false once the sequence is exhausted.
+struct TileCursor {
+    WorkIter w;
+    Item x;
+    int t;
+    SDB_DEV explicit TileCursor(const Params& p) : w(p), t(-1) {
+        if (w.valid()) x = w.item(p);
+        advance(p);
+    }
+    SDB_DEV bool valid() const { return w.valid(); }
+    SDB_DEV void advance(const Params& p) {
         ++t;
-        while (it < total_items && t >= x.ntiles) {
-            it += gridDim.x;
+        while (w.valid() && t >= x.ntiles) {
+            w.next(p, x);
             t = 0;
-            if (it < total_items) x = item_at(p, it);
+            if (w.valid()) x = w.item(p);
         }
     }
 };
@@ -152,7 +204,7 @@ SDB_DEV float transpose_reduce16(float (&v)[16], int lane) {
 template <typename T>
 __global__ void __launch_bounds__(THREADS, 1)
     pa_umma_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
-                   const __grid_constant__ CUtensorMap qmap, const Params p, int total_items) {
+                   const __grid_constant__ CUtensorMap qmap, const Params p) {
     using H = Half16<T>;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -163,6 +215,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     float* red_max = reinterpret_cast<float*>(smem + OFF_RED);
     float* red_sum = red_max + 4 * 32;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // the split merge (a programmatic dependent launch) may become resident now; it
+    // waits for this grid's completion before reading anything
+    asm volatile("griddepcontrol.launch_dependents;");
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < UNS; ++s) {
@@ -204,8 +259,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             const uint64_t qpol = l2_policy_evict_normal();  // every split of a sequence reads Q
             int gt = 0, nq = 0;
             bool ok = true;
-            TileCursor ld(p, blockIdx.x, total_items);
-            while (ld.it < total_items) {
+            TileCursor ld(p);
+            while (ld.valid()) {
                 const int j = ld.x.k0 + ld.t * UBN;
                 // the block id is read before the waits, off the stage-hold path
                 int blk = p.bt[(int64_t)ld.x.b * p.bt_stride + j / p.page];
@@ -242,7 +297,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 tma_load_4d(vdst, &vmap, fb, 0, ld.x.kvh, off, blk, pol);
                 tma_load_4d(vdst + UHALF, &vmap, fb, 64, ld.x.kvh, off, blk, pol);
                 ++gt;
-                ld.advance(p, total_items);
+                ld.advance(p);
             }
             if (!ok) atomicOr(p.err, SDB_KERR_TIMEOUT);
             for (int g = gt - UNS > 0 ? gt - UNS : 0; g < gt; ++g) {  // drain own copies
@@ -267,7 +322,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             int gt = 0, nitem = 0;
             bool ok = true;
             // O^T += V(g)^T . P(g), heads and residuals as N = 64; completion frees stage g (K, V and P)
-            auto pv = [&](int g, bool first) -> bool {
+            auto pv = [&](int g, bool first, uint32_t ocol) -> bool {
                 if (!mbar_wait(bar.pfull, g & 1)) return false;
                 tc_fence_after();
                 const uint32_t stage = sbase + (g % UNS) * USTAGE;
@@ -276,20 +331,22 @@ __global__ void __launch_bounds__(THREADS, 1)
                 for (int ks = 0; ks < 8; ++ks) {
                     const uint64_t a = sdesc_sw128(vbase + ks * 2048, UHALF, 1024);
                     const uint64_t b = sdesc_sw128(stage + ks * 2048, UHALF, 1024);
-                    umma_f16_ss(tmem + 64, a, b, IDESC_PV, (first && ks == 0) ? 0u : 1u);
+                    umma_f16_ss(tmem + ocol, a, b, IDESC_PV, (first && ks == 0) ? 0u : 1u);
                 }
                 umma_commit(bar.empty0 + 8 * (g % UNS));
                 return true;
             };
             // nitem counts the items that have tiles: only those take a Q buffer / q_ready phase
-            for (int it = blockIdx.x; it < total_items && ok; it += gridDim.x) {
-                const Item x = item_at(p, it);
+            for (WorkIter w(p); w.valid() && ok;) {
+                const Item x = w.item(p);
+                w.next(p, x);
                 if (x.ntiles == 0) continue;
                 if (!mbar_wait(bar.qready0 + 8 * (nitem & 1), (nitem >> 1) & 1)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
+                const uint32_t ocol = TCOL_O;
                 for (int t = 0; t < x.ntiles; ++t, ++gt) {
                     const int s = gt % UNS, sb = gt & 1;
                     if (!mbar_wait(bar.full0 + 8 * s, (gt / UNS) & 1) ||
@@ -308,12 +365,12 @@ __global__ void __launch_bounds__(THREADS, 1)
                     }
                     umma_commit(bar.sfull0 + 8 * sb);
                     if (t == x.ntiles - 1) umma_commit(bar.qfree0 + 8 * (nitem & 1));  // Q buffer read
-                    if (t >= 1 && !pv(gt - 1, t == 1)) {
+                    if (t >= 1 && !pv(gt - 1, t == 1, ocol)) {
                         ok = false;
                         break;
                     }
                 }
-                if (ok && !pv(gt - 1, x.ntiles == 1)) ok = false;
+                if (ok && !pv(gt - 1, x.ntiles == 1, ocol)) ok = false;
                 ++nitem;
             }
             if (!ok) atomicOr(p.err, SDB_KERR_TIMEOUT);
@@ -343,8 +400,52 @@ __global__ void __launch_bounds__(THREADS, 1)
         int gt = 0;
         bool ok = true;
         T* obase = reinterpret_cast<T*>(p.out);
-        for (int it = blockIdx.x; it < total_items; it += gridDim.x) {
-            const Item x = item_at(p, it);
+        // Result of an item of pair `pair` for columns cb .. cb+7 (cb = c0 or c0 + 8): the
+        // output rows (slot < 0: the CTA saw every key of the pair) or partial `slot` of
+        // the pair: O^T column c, the row max reference and the row sum.
+        auto store8 = [&](int pair, int slot, int cb, const float (&o)[8], float lsum, float mb_own) {
+            const int dim = 32 * qt + lane;
+            if (slot < 0) {
+                const int b = pair / p.Hkv, kvh = pair - b * p.Hkv;
+                int r = cb / p.G, g = cb % p.G;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const float l_i = __shfl_sync(0xffffffffu, lsum, cb - c0 + i);
+                    if (cb + i < R) {
+                        T* dst = obase + (int64_t)(b * p.n_q + r) * p.o_srow +
+                                 (int64_t)(kvh * p.G + g) * p.o_shead + dim;
+                        *dst = from_f32<T>(l_i > 0.f ? o[i] / l_i : 0.f);
+                    }
+                    if (++g == p.G) {
+                        g = 0;
+                        ++r;
+                    }
+                }
+                return;
+            }
+            const int64_t sl = (int64_t)pair * p.splits + slot;
+            float* po = p.part_o + sl * R * D;
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                if (cb + i < R) __stcg(po + (cb + i) * D + dim, o[i]);
+            if (cb == c0 && qt == 0 && lane < 16 && c0 + lane < R)
+                __stcg(reinterpret_cast<float2*>(p.part_ml + (sl * R + c0 + lane) * 2), make_float2(mb_own, lsum));
+        };
+        for (WorkIter w(p); w.valid();) {
+            const Item x = w.item(p);
+            w.next(p, x);
+            const int pair = x.b * p.Hkv + x.kvh;
+            const int slot = x.direct ? -1 : x.slot;
+            if (x.ntiles == 0) {
+                // no keys: zero output or an empty partial (m = -inf, l = 0)
+                float o[8];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) o[i] = 0.f;
+                store8(pair, slot, c0, o, 0.f, NEG_INF);
+                store8(pair, slot, c0 + 8, o, 0.f, NEG_INF);
+                continue;
+            }
+            const uint32_t ocol = TCOL_O;
 
             float mb_own = NEG_INF;   // reference of column c0 + lc
             float mbv[16], lpart[16];
@@ -414,16 +515,16 @@ __global__ void __launch_bounds__(THREADS, 1)
                         wait_or_skip(bar.empty0 + 8 * (g1 % UNS), (g1 / UNS) & 1, ok);
                         tc_fence_after();
                         uint32_t oh[16], ol[16];
-                        tmem_ld16(tmem + lane_addr + 64 + c0, oh);
-                        tmem_ld16(tmem + lane_addr + 96 + c0, ol);
+                        tmem_ld16(tmem + lane_addr + ocol + c0, oh);
+                        tmem_ld16(tmem + lane_addr + ocol + 32 + c0, ol);
                         tmem_wait_ld();
 #pragma unroll
                         for (int i = 0; i < 16; ++i) {
                             oh[i] = __float_as_uint(__uint_as_float(oh[i]) * av[i]);
                             ol[i] = __float_as_uint(__uint_as_float(ol[i]) * av[i]);
                         }
-                        tmem_st16(tmem + lane_addr + 64 + c0, oh);
-                        tmem_st16(tmem + lane_addr + 96 + c0, ol);
+                        tmem_st16(tmem + lane_addr + ocol + c0, oh);
+                        tmem_st16(tmem + lane_addr + ocol + 32 + c0, ol);
                         tmem_wait_st();
                     }
                 }
@@ -465,61 +566,35 @@ __global__ void __launch_bounds__(THREADS, 1)
                 if (lane == 0) mbar_arrive(bar.pfull);
             }
 
+
             // ---- item epilogue: row sums, then O^T column c is row c (this thread: dim 32*qt + lane)
             float lsum;
             {
                 const float ws = transpose_reduce16<false>(lpart, lane);
-                // every warp has read the previous item's red_sum (an item without tiles
-                // reaches this point with no vote barrier in between)
+                // every warp has read the previous item's red_sum
                 named_barrier_sync(1, SOFTMAX_THREADS);
                 if (lane < 16) red_sum[qt * 32 + c0 + lane] = ws;
                 named_barrier_sync(1, SOFTMAX_THREADS);
                 const int cc = c0 + lc;
                 lsum = (red_sum[cc] + red_sum[32 + cc]) + (red_sum[64 + cc] + red_sum[96 + cc]);
             }
-            float o[16];
-            if (x.ntiles > 0) {
-                const int g1 = gt - 1;
-                wait_or_skip(bar.empty0 + 8 * (g1 % UNS), (g1 / UNS) & 1, ok);
-                tc_fence_after();
+            // the last P.V (it frees the last stage) has completed: O^T is final
+            const int g1 = gt - 1;
+            wait_or_skip(bar.empty0 + 8 * (g1 % UNS), (g1 / UNS) & 1, ok);
+            tc_fence_after();
+            {
                 uint32_t oh[16], ol[16];
-                tmem_ld16(tmem + lane_addr + 64 + c0, oh);
-                tmem_ld16(tmem + lane_addr + 96 + c0, ol);
+                tmem_ld16(tmem + lane_addr + ocol + c0, oh);
+                tmem_ld16(tmem + lane_addr + ocol + 32 + c0, ol);
                 tmem_wait_ld();
 #pragma unroll
-                for (int i = 0; i < 16; ++i) o[i] = __uint_as_float(oh[i]) + __uint_as_float(ol[i]);
-            } else {
+                for (int h = 0; h < 2; ++h) {
+                    float o[8];
 #pragma unroll
-                for (int i = 0; i < 16; ++i) o[i] = 0.f;
-            }
-            const int dim = 32 * qt + lane;
-            if (p.splits == 1) {
-                int r = c0 / p.G, g = c0 % p.G;
-#pragma unroll
-                for (int i = 0; i < 16; ++i) {
-                    const float l_i = __shfl_sync(0xffffffffu, lsum, i);
-                    if (c0 + i < R) {
-                        T* dst = obase + (int64_t)(x.b * p.n_q + r) * p.o_srow +
-                                 (int64_t)(x.kvh * p.G + g) * p.o_shead + dim;
-                        *dst = from_f32<T>(l_i > 0.f ? o[i] / l_i : 0.f);
-                    }
-                    if (++g == p.G) {
-                        g = 0;
-                        ++r;
-                    }
+                    for (int i = 0; i < 8; ++i) o[i] = __uint_as_float(oh[8 * h + i]) + __uint_as_float(ol[8 * h + i]);
+                    store8(pair, slot, c0 + 8 * h, o, lsum, mb_own);
                 }
-                continue;
             }
-            const int pair = x.b * p.Hkv + x.kvh;
-            const int64_t slot = (int64_t)pair * p.splits + x.split;
-            float* po = p.part_o + slot * R * D;
-            float* pml = p.part_ml + slot * R * 2;
-#pragma unroll
-            for (int i = 0; i < 16; ++i)
-                if (c0 + i < R) __stcg(po + (c0 + i) * D + dim, o[i]);
-            if (qt == 0 && lane < 16 && c0 + lane < R)
-                __stcg(reinterpret_cast<float2*>(pml + (c0 + lane) * 2), make_float2(mb_own, lsum));
-            // the LSE merge of the splits runs as a separate kernel (pa_umma_merge_kernel)
         }
         if (!ok && lane == 0) atomicOr(p.err, SDB_KERR_TIMEOUT);
     }
@@ -530,63 +605,68 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (warp == 1) tmem_dealloc(tmem, TMEM_COLS);
 }
 
-// LSE merge of the split partials: one CTA per (sequence, kv head), one thread per
-// dim; per-split weights exp2(m_s - M) / L computed once per row into shared memory.
+// LSE merge of the split partials.  One thread per (pair, row, 4 dims): out =
+// sum_s w_s o_s with w_s = 2^(m_s - M) / sum_s 2^(m_s - M) l_s over the pair's
+// partials (independent L2 reads).  Under the balanced partition only sequences cut
+// by a group boundary have partials; the grid covers just those.  Launched as a programmatic dependent of pa_umma_kernel:
+// its CTAs become resident while the attention tail runs and wait
+// (griddepcontrol.wait) for its results.
+constexpr int MERGE_THREADS = 128;  // small enough to sit beside a pa_umma_kernel CTA
 template <typename T>
-__global__ void __launch_bounds__(128) pa_umma_merge_kernel(const Params p) {
-    __shared__ float W[kMaxUmmaSplits][NROW];
-    const int pair = blockIdx.x;
-    const int b = pair / p.Hkv, kvh = pair % p.Hkv;
+__global__ void __launch_bounds__(MERGE_THREADS) pa_umma_merge_kernel(const Params p) {
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int R = p.R;
-    const float* ml = p.part_ml + (int64_t)pair * p.splits * R * 2;
-    const float* pob = p.part_o + (int64_t)pair * p.splits * R * D;
-    const int t = threadIdx.x;
-    if (t < R) {
-        float mv[kMaxUmmaSplits], lv[kMaxUmmaSplits];
-        float Mx = NEG_INF;
-#pragma unroll
-        for (int s2 = 0; s2 < kMaxUmmaSplits; ++s2)
-            if (s2 < p.splits) {
-                const float2 v = *reinterpret_cast<const float2*>(ml + (s2 * R + t) * 2);
-                mv[s2] = v.x;
-                lv[s2] = v.y;
-                Mx = fmaxf(Mx, v.x);
-            }
-        const float Bm = Mx == NEG_INF ? 0.f : Mx;
-        float Ls = 0.f;
-#pragma unroll
-        for (int s2 = 0; s2 < kMaxUmmaSplits; ++s2)
-            if (s2 < p.splits) {
-                mv[s2] = ex2(mv[s2] - Bm);
-                Ls += mv[s2] * lv[s2];
-            }
-        const float inv = Ls > 0.f ? 1.f / Ls : 0.f;
-#pragma unroll
-        for (int s2 = 0; s2 < kMaxUmmaSplits; ++s2)
-            if (s2 < p.splits) W[s2][t] = mv[s2] * inv;
-    }
-    __syncthreads();
-    T* obase = reinterpret_cast<T*>(p.out);
-    int r = 0, g = 0;
-    for (int c0 = 0; c0 < R; c0 += 8) {
-        float acc[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-        for (int s2 = 0; s2 < p.splits; ++s2)
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-                if (c0 + i < R) acc[i] += W[s2][c0 + i] * pob[((int64_t)s2 * R + c0 + i) * D + t];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            if (c0 + i < R)
-                obase[(int64_t)(b * p.n_q + r) * p.o_srow + (int64_t)(kvh * p.G + g) * p.o_shead + t] =
-                    from_f32<T>(acc[i]);
-            if (++g == p.G) {
-                g = 0;
-                ++r;
-            }
+    const int rb = (R * 32 + MERGE_THREADS - 1) / MERGE_THREADS;  // CTAs per pair
+    const int u = (blockIdx.y % rb) * MERGE_THREADS + threadIdx.x;  // row * 32 + dim quad
+    const int c = u >> 5, dq = u & 31;
+    if (c >= R) return;
+    int pair, nseg;
+    if (p.flat_T > 0) {
+        // grid.x: group boundaries 1 .. groups-1; the first boundary inside a sequence
+        // merges it (grid.y: kv head x row block)
+        const int k = blockIdx.x + 1;
+        const long long f = flat_start(p, k);
+        const long long b = f / p.flat_T;
+        if (f % p.flat_T == 0) return;
+        if (k > 1) {
+            const long long fp = flat_start(p, k - 1);
+            if (fp / p.flat_T == b && fp % p.flat_T != 0) return;
         }
+        pair = (int)b * p.Hkv + (int)blockIdx.y / rb;
+        nseg = flat_group_of(p, (b + 1) * p.flat_T - 1) - flat_group_of(p, b * p.flat_T) + 1;
+    } else {
+        pair = blockIdx.x;  // grid.y: row blocks
+        nseg = p.splits;
     }
+    const float* ml = p.part_ml + (int64_t)pair * p.splits * R * 2 + c * 2;
+    const float4* po = reinterpret_cast<const float4*>(p.part_o + (int64_t)pair * p.splits * R * D + c * D) + dq;
+    const int64_t sstride = (int64_t)R * D / 4;  // float4s between partials
+    float Mx = NEG_INF;
+#pragma unroll 4
+    for (int s2 = 0; s2 < nseg; ++s2) Mx = fmaxf(Mx, __ldcg(ml + s2 * R * 2));
+    const float Bm = Mx == NEG_INF ? 0.f : Mx;
+    float Ls = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 4
+    for (int s2 = 0; s2 < nseg; ++s2) {
+        const float2 v = __ldcg(reinterpret_cast<const float2*>(ml + s2 * R * 2));
+        const float4 o = __ldcg(po + s2 * sstride);
+        const float w = ex2(v.x - Bm);
+        Ls += w * v.y;
+        acc.x += w * o.x;
+        acc.y += w * o.y;
+        acc.z += w * o.z;
+        acc.w += w * o.w;
+    }
+    const float inv = Ls > 0.f ? 1.f / Ls : 0.f;
+    const int b = pair / p.Hkv, kvh = pair % p.Hkv;
+    const int r = c / p.G, g = c % p.G;
+    T* dst = reinterpret_cast<T*>(p.out) + (int64_t)(b * p.n_q + r) * p.o_srow +
+             (int64_t)(kvh * p.G + g) * p.o_shead + dq * 4;
+    dst[0] = from_f32<T>(acc.x * inv);
+    dst[1] = from_f32<T>(acc.y * inv);
+    dst[2] = from_f32<T>(acc.z * inv);
+    dst[3] = from_f32<T>(acc.w * inv);
 }
 
 }  // namespace umma
@@ -596,39 +676,109 @@ bool umma_path(int dtype, int D_, int page, int R) {
     return (dtype == SDB_BF16 || dtype == SDB_F16) && D_ == D && page % umma::UBN == 0 && R <= umma::NROW;
 }
 
-// Splits for the persistent grid: minimise (items per CTA) x (tiles per item), from static shape only.
-int pick_umma_splits(int B, int R, int Hkv, int page, int max_blocks, int sms) {
+// Balanced partition geometry from the static shape: tile slots per sequence, all
+// slots, CTA groups, and the most groups one sequence can straddle (the partial slots
+// a pair needs).  groups == 0: the kv heads do not fit the SMs as groups.
+struct FlatShape {
+    int T, groups, slots;
+    long long total;
+};
+static FlatShape flat_shape(int B, int Hkv, int page, int max_blocks, int sms) {
+    FlatShape f;
     const long long max_ctx = (long long)max_blocks * page;
-    const long long tiles = (max_ctx + umma::UBN - 1) / umma::UBN;
+    f.T = (int)((max_ctx + umma::UBN - 1) / umma::UBN);
+    if (f.T < 1) f.T = 1;
+    f.total = (long long)B * f.T;
+    const long long g = sms / Hkv;
+    f.groups = (int)(f.total < g ? f.total : g);
+    if (f.groups < 1) {
+        f.groups = 0;
+        f.slots = 1;
+        return f;
+    }
+    const long long m = f.total / f.groups;  // shortest group range, >= 1
+    long long slots = (f.T + m - 1) / m + 1;
+    if (slots > f.groups) slots = f.groups;
+    f.slots = (int)slots;
+    return f;
+}
+
+// Decomposition choice from the static shape, in tile-time units: the strided split
+// count s costs its busiest CTA's tiles plus kItemCost per item it runs and, with
+// s > 1, the merge (growing with the partials per pair); the grouped partition costs its (even) tiles per CTA times
+// kGroupedTax (measured: its CTAs stream somewhat slower than the strided ones),
+// its items and the merge.  Fitted to B200 runs of Qwen3-shaped verify / decode
+// batches (B 16..128, context 2K..8K).
+struct UmmaPlan {
+    bool grouped;
+    int splits;  // partial slots per pair (grouped) or the strided split count
+};
+static UmmaPlan umma_plan(int B, int Hkv, int page, int max_blocks, int sms) {
+    constexpr double kItemCost = 1.0, kMergeBase = 1.5, kMergePerSlot = 0.25, kGroupedTax = 1.08;
+    const FlatShape fs = flat_shape(B, Hkv, page, max_blocks, sms);
     const long long pairs = (long long)B * Hkv;
-    int best = 1;
+    UmmaPlan best{false, 1};
     double best_cost = 1e300;
     for (int s = 1; s <= umma::kMaxUmmaSplits; ++s) {
-        const long long chunk_tiles = (tiles + s - 1) / s;
-        if (s > 1 && chunk_tiles < 2) break;
-        const long long items = pairs * s;
+        const long long chunk = (fs.T + s - 1) / s;
+        if (s > 1 && chunk < 2) break;
+        const long long s_eff = (fs.T + chunk - 1) / chunk;
+        if (s > 1 && s_eff < s) continue;  // same as a smaller s
+        const long long items = pairs * s_eff;
         const long long grid = items < sms ? items : sms;
         const long long per_cta = (items + grid - 1) / grid;
-        double cost = (double)per_cta * (chunk_tiles * (double)umma::USTAGE + 4096.0);
-        if (s > 1) cost += (double)per_cta * R * (D + 2) * 8.0;
-        if (cost < best_cost * 0.995) {
+        const double cost = per_cta * (chunk + kItemCost) + (s_eff > 1 ? kMergeBase + kMergePerSlot * s_eff : 0.0);
+        if (cost < best_cost) {
             best_cost = cost;
-            best = s;
+            best = UmmaPlan{false, (int)s_eff};
         }
+    }
+    if (fs.groups > 0) {
+        const double tiles = (double)((fs.total + fs.groups - 1) / fs.groups);
+        const double items = tiles / fs.T + 1.0;
+        const double cost =
+            tiles * kGroupedTax + items * kItemCost + (fs.groups > 1 ? kMergeBase + kMergePerSlot * fs.slots : 0.0);
+        if (cost < best_cost) best = UmmaPlan{true, fs.slots};
     }
     return best;
 }
 
+// Default `splits` of the tcgen05 path: the partial slots per pair its plan needs.
+int pick_umma_splits(int B, int, int Hkv, int page, int max_blocks, int sms) {
+    return umma_plan(B, Hkv, page, max_blocks, sms).splits;
+}
+
+// `splits` is the partial-slot capacity per pair.  The grouped partition runs when the
+// plan prefers it and the capacity covers it; otherwise every pair is split into
+// `splits` key chunks, strided over the persistent CTAs.
 int launch_umma(const void* k_cache, const void* v_cache, int dtype, int64_t sb, int64_t sp, int64_t sh,
                 Params& p, void* workspace, size_t workspace_bytes, int splits, cudaStream_t st) {
     const int sms = device_sm_count();
-    if (splits <= 0) splits = pick_umma_splits(p.B, p.R, p.Hkv, p.page, p.max_blocks, sms);
-    if (splits > umma::kMaxUmmaSplits) splits = umma::kMaxUmmaSplits;
-    const long long max_ctx = (long long)p.max_blocks * p.page;
-    long long chunk = ((max_ctx + splits - 1) / splits + umma::UBN - 1) / umma::UBN * umma::UBN;
-    if (chunk < umma::UBN) chunk = umma::UBN;
-    splits = (int)((max_ctx + chunk - 1) / chunk);
-    if (splits < 1) splits = 1;
+    const FlatShape fs = flat_shape(p.B, p.Hkv, p.page, p.max_blocks, sms);
+    const UmmaPlan plan = umma_plan(p.B, p.Hkv, p.page, p.max_blocks, sms);
+    if (splits <= 0) splits = plan.splits;
+    int grid;
+    bool merge;
+    if (plan.grouped && splits >= fs.slots && fs.total < (1LL << 31)) {
+        p.flat_T = fs.T;
+        p.flat_total = fs.total;
+        p.flat_grid = fs.groups;
+        p.chunk = 0;
+        grid = fs.groups * p.Hkv;
+        merge = fs.groups > 1;
+    } else {
+        if (splits > umma::kMaxUmmaSplits) splits = umma::kMaxUmmaSplits;
+        const long long max_ctx = (long long)p.max_blocks * p.page;
+        long long chunk = ((max_ctx + splits - 1) / splits + umma::UBN - 1) / umma::UBN * umma::UBN;
+        if (chunk < umma::UBN) chunk = umma::UBN;
+        splits = (int)((max_ctx + chunk - 1) / chunk);
+        if (splits < 1) splits = 1;
+        p.flat_T = 0;
+        p.chunk = (int)chunk;
+        const long long items = (long long)p.B * p.Hkv * splits;
+        grid = (int)(items < sms ? items : sms);
+        merge = splits > 1;
+    }
     WsLayout w = ws_layout(p.B, p.R, p.Hkv, splits);
     if (workspace_bytes < w.total) {
         set_last_error("workspace too small: need %zu bytes, got %zu", w.total, workspace_bytes);
@@ -640,7 +790,6 @@ int launch_umma(const void* k_cache, const void* v_cache, int dtype, int64_t sb,
     p.part_ml = reinterpret_cast<float*>(ws + w.part_ml);
     p.part_o = reinterpret_cast<float*>(ws + w.part_o);
     p.splits = splits;
-    p.chunk = (int)chunk;
     const CUtensorMapDataType dt = dtype == SDB_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)p.Hkv, (cuuint64_t)p.page, (cuuint64_t)p.num_blocks};
     cuuint64_t strides[3] = {(cuuint64_t)sh * 2, (cuuint64_t)sp * 2, (cuuint64_t)sb * 2};
@@ -659,24 +808,33 @@ int launch_umma(const void* k_cache, const void* v_cache, int dtype, int64_t sb,
     CUtensorMap qm;
     rc = encode_tensor_map(&qm, dt, 4, const_cast<void*>(p.q), qdims, qstrides, qbox, CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
-    const int total_items = p.B * p.Hkv * splits;
-    const int grid = total_items < sms ? total_items : sms;
     if (dtype == SDB_BF16) {
         auto kern = umma::pa_umma_kernel<__nv_bfloat16>;
         rc = ensure_smem_attr(reinterpret_cast<const void*>(kern), umma::SMEM_BYTES, 40);
         if (rc) return rc;
-        kern<<<grid, umma::THREADS, umma::SMEM_BYTES, st>>>(km, vm, qm, p, total_items);
+        kern<<<grid, umma::THREADS, umma::SMEM_BYTES, st>>>(km, vm, qm, p);
     } else {
         auto kern = umma::pa_umma_kernel<__half>;
         rc = ensure_smem_attr(reinterpret_cast<const void*>(kern), umma::SMEM_BYTES, 41);
         if (rc) return rc;
-        kern<<<grid, umma::THREADS, umma::SMEM_BYTES, st>>>(km, vm, qm, p, total_items);
+        kern<<<grid, umma::THREADS, umma::SMEM_BYTES, st>>>(km, vm, qm, p);
     }
     rc = cuda_status(cudaGetLastError(), "pa_umma_kernel launch");
-    if (rc || splits == 1) return rc;
-    if (dtype == SDB_BF16) umma::pa_umma_merge_kernel<__nv_bfloat16><<<p.B * p.Hkv, 128, 0, st>>>(p);
-    else umma::pa_umma_merge_kernel<__half><<<p.B * p.Hkv, 128, 0, st>>>(p);
-    return cuda_status(cudaGetLastError(), "pa_umma_merge_kernel launch");
+    if (rc || !merge) return rc;
+    cudaLaunchConfig_t cfg = {};
+    const int rb = (p.R * 32 + umma::MERGE_THREADS - 1) / umma::MERGE_THREADS;
+    cfg.gridDim = p.flat_T > 0 ? dim3(p.flat_grid - 1, p.Hkv * rb, 1) : dim3(p.B * p.Hkv, rb, 1);
+    cfg.blockDim = dim3(umma::MERGE_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = dtype == SDB_BF16 ? cudaLaunchKernelEx(&cfg, umma::pa_umma_merge_kernel<__nv_bfloat16>, p)
+                                      : cudaLaunchKernelEx(&cfg, umma::pa_umma_merge_kernel<__half>, p);
+    return cuda_status(e, "pa_umma_merge_kernel launch");
 }
 
 }  // namespace attn
