@@ -72,8 +72,14 @@ const char* sdb_build_info(void);
  * dtype: SDB_BF16 / SDB_F16 (tensor-core path: D = 128, page % 64 == 0,
  *        n_q*Hq/Hkv <= 64) or SDB_F32 (CUDA-core path, fp32 accumulate, any
  *        page, D in {32, 64, 128, 256}, n_q*Hq/Hkv <= 64).  B * Hkv <= 65536.
- * splits: KV splits per (sequence, kv head); 0 picks a default from the static
- *         shape (max_blocks * page), never from device data.
+ * splits: partial slots per (sequence, kv head) the workspace is sized for; 0
+ *         picks sdb_paged_attention_default_splits().  The decomposition is chosen
+ *         from the static shape (max_blocks * page), never from device data: with
+ *         16-bit KV, D = 128, page % 128 == 0 and n_q*Hq/Hkv <= 32 (tcgen05 kernel)
+ *         either every pair is split into `splits` key chunks, or -- when the
+ *         shape plan prefers it and `splits` covers it -- a balanced partition of
+ *         all keys over groups of CTAs that splits only pairs cut by a group
+ *         boundary; on the other paths `splits` is the key-chunk count.
  * workspace: sdb_paged_attention_workspace_size() bytes, 256-byte aligned,
  *         zero-filled once before first use (the kernels leave it re-usable).
  * ========================================================================= */
