@@ -69,6 +69,28 @@ SDB_DEV bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     return ok != 0;
 }
 
+// try_wait with a suspend-time hint: a thread whose phase is not complete sleeps in the
+// barrier (woken by the completing arrival) instead of spinning; for waits on HBM.
+SDB_DEV bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "n"(1000000)
+        : "memory");
+    return ok != 0;
+}
+SDB_DEV bool mbar_wait_sleep(uint32_t bar, uint32_t parity) {
+    if (mbar_try_wait_sleep(bar, parity)) return true;
+    const long long t0 = clock64();
+    while (!mbar_try_wait_sleep(bar, parity)) {
+        if (clock64() - t0 > kSpinLimitCycles) return false;
+    }
+    return true;
+}
+
 // Wait for the phase of the given parity to complete; false after ~2 s.
 SDB_DEV bool mbar_wait(uint32_t bar, uint32_t parity) {
     if (mbar_try_wait(bar, parity)) return true;
@@ -88,6 +110,16 @@ SDB_DEV void tma_load_4d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int
         " [%0], [%1, {%3, %4, %5, %6}], [%2], %7;" ::"r"(dst),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3),
         "l"(policy)
+        : "memory");
+}
+
+// Contiguous bulk copy global -> this CTA's shared memory, completing on an mbarrier
+// (both addresses 16-byte aligned, bytes a multiple of 16).  No multicast.
+SDB_DEV void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+            dst),
+        "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar), "l"(policy)
         : "memory");
 }
 

@@ -1,20 +1,20 @@
 // verify_batch rejection sampling on B200 (sm_100a).
 //
-// Reference: nanovllm/spec_decode/verify.py:42-209.  Same arithmetic, three
+// Reference: nanovllm/spec_decode/verify.py:42-209.  Same arithmetic, four
 // launches instead of ~8 passes of generic torch kernels plus a q_pad copy:
 //
-//   1. vs_row_stats   grid (rows, chunks): per chunk of every draft and target
-//      row, max and sum of exp(x/T - max) from values held in registers
-//      (one HBM read of every logit -- the floor of this path).
-//   2. vs_resid_sums  grid (B, chunks): every CTA merges the row statistics of
-//      its sequence, recomputes the k acceptance decisions (candidate j against
-//      target row j, ratio = min(1, p/q), u < ratio, verify.py:109-129) and sums
-//      resid = max(p[a] - q_pad[a], 0) and p[a] over its chunk of row a = accepted
-//      (verify.py:141-151).
-//   3. vs_bonus       grid (B, chunks): partial argmax of (resid / Z) / max(E, 1e-10)
+//   1. vs_row_stats   grid (rows, chunks of 8192): per chunk of every draft and
+//      target row, max and sum of exp(x/T - max) (one HBM read of every logit --
+//      the floor of this path; 32 logits per thread held in registers).
+//   2. vs_decide      one warp per sequence: merges the row statistics and makes
+//      the k acceptance decisions (candidate j against target row j, ratio =
+//      min(1, p/q), u < ratio, verify.py:109-129).
+//   3. vs_resid_sums  grid (B, chunks): sums resid = max(p[a] - q_pad[a], 0) and
+//      p[a] over its chunk of row a = accepted (verify.py:141-151).
+//   4. vs_bonus       grid (B, chunks): partial argmax of (resid / Z) / max(E, 1e-10)
 //      (verify.py:152, :167, :203-209), first index on ties; the last CTA of a
 //      sequence (atomic counter, reset after use) finishes the argmax and writes
-//      accepted / accept_mask / bonus.
+//      the bonus token.
 //
 // The draws: acceptance uniforms u[b, j] and exponentials E[b, i] are either
 // caller-provided (parity with the reference given identical draws) or
@@ -24,6 +24,7 @@
 // sequence of correctly rounded float32 operations (no contraction) so a CPU
 // restatement reproduces every bit.
 #include <cfloat>
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -31,9 +32,18 @@ namespace sdb {
 namespace vs {
 
 constexpr int THREADS = 256;
-constexpr int EPT = 64;                    // logits per thread held in registers (pass 1)
-constexpr int CHUNK1 = THREADS * EPT;      // 16384 logits per CTA in pass 1
-constexpr int CHUNK2 = THREADS * 32;       // 8192 logits per CTA in passes 2-3
+constexpr int EPT = 32;                    // logits per thread held in registers (pass 1)
+constexpr int CHUNK1 = THREADS * EPT;      // 8192 logits per chunk in pass 1
+constexpr int EPT2 = 16;                   // logits per thread in passes 3-4
+constexpr int CHUNK2 = THREADS * EPT2;     // 4096 logits per CTA in passes 3-4
+// pass 1, streaming form: persistent CTAs, one producer warp moving 32 KB chunks of
+// a row into a shared-memory ring by bulk copy, 16 consumer warps reducing them
+constexpr int SUB = 16;                    // (max, sum) partials per chunk: one per consumer warp
+constexpr int BS_STAGES = 3;               // x 32 KB, two CTAs per SM
+constexpr int BS_CONSUMERS = SUB;          // warps, 512 logits of each chunk apiece
+constexpr int BS_EPT = CHUNK1 / (32 * BS_CONSUMERS);
+constexpr int BS_THREADS = 32 * (BS_CONSUMERS + 1);
+constexpr int BS_SMEM = BS_STAGES * CHUNK1 * 4;
 
 struct Params {
     const float* draft;    // (B, k, V)
@@ -48,7 +58,7 @@ struct Params {
     int64_t* out_bonus;
     uint8_t* out_mask;
     int B, k, Tr, V, C1, C2;
-    float2* stats;         // [rows][C1]  (max, sumexp)
+    float2* stats;         // [rows][C1 * SUB]  (max, sumexp) per chunk and warp
     float2* rsum;          // [B][C2]     (sum resid, sum p[a])
     float2* amax;          // [B][C2]     (value, index as float bits)
     int* counters;         // [B], zero between calls
@@ -112,17 +122,6 @@ SDB_DEV float log_fixed(float x) {
     return __fadd_rn(__fmul_rn(ef, ln2_hi), __fadd_rn(lm, __fmul_rn(ef, ln2_lo)));
 }
 
-SDB_DEV float exp_noise(const Params& p, int b, int i) {
-    float E;
-    if (p.e) {
-        E = p.e[(int64_t)b * p.V + i];
-    } else {
-        const uint32_t w = philox_word(p.seed_lo, p.seed_hi, p.offset, 1u, (uint32_t)b, (uint32_t)i);
-        E = -log_fixed(word_to_open_uniform(w));
-    }
-    return fmaxf(E, 1e-10f);  // clamp_min_(1e-10), verify.py:209
-}
-
 SDB_DEV float accept_uniform(const Params& p, int b, int j) {
     if (p.u) return p.u[b * p.k + j];
     return word_to_uniform(philox_word(p.seed_lo, p.seed_hi, p.offset, 0u, (uint32_t)b, (uint32_t)j));
@@ -152,75 +151,11 @@ struct Decision {
     float Mq, iq;   // same for draft row a (a < k, not point mass)
 };
 
-// Merged (max, 1/sum) of one row from its per-chunk statistics.
-SDB_DEV void row_norm(const Params& p, int row, float& M, float& inv) {
-    const float2* st = p.stats + (int64_t)row * p.C1;
-    M = -INFINITY;
-    for (int c = 0; c < p.C1; ++c) M = fmaxf(M, __ldcg(st + c).x);
-    float S = 0.f;
-    for (int c = 0; c < p.C1; ++c) {
-        const float2 v = __ldcg(st + c);
-        if (v.x != -INFINITY) S += v.y * expf(v.x - M);
-    }
-    inv = 1.0f / S;
-}
-
-// The k acceptance decisions of sequence b, one candidate per lane (warp-wide).
-// ratio = where(q_tok > 0, min(p_tok / max(q_tok, 1e-10), 1), 0); accept = u < ratio
-// (verify.py:109-121); accepted = first rejection or k (:125-129).
-SDB_DEV void decide_warp(const Params& p, int b, Decision* out) {
-    const int lane = threadIdx.x & 31;
-    const int nd = p.B * p.k;
-    const float T = p.temps ? p.temps[b] : 1.0f;
-    bool acc = true;
-    if (lane < p.k) {
-        int64_t tok = p.tokens[b * p.k + lane];
-        if (tok < 0 || tok >= p.V) {
-            atomicOr(p.err, SDB_KERR_TOKEN);
-            tok = 0;
-        }
-        const int drow = b * p.k + lane;
-        float q_tok;
-        if (p.point_mass) {
-            q_tok = p.draft[(int64_t)drow * p.V + tok];
-        } else {
-            float M, inv;
-            row_norm(p, drow, M, inv);
-            q_tok = expf(scale_t(p.draft[(int64_t)drow * p.V + tok], T) - M) * inv;
-        }
-        float Mt, it;
-        row_norm(p, nd + b * p.Tr + lane, Mt, it);
-        const float p_tok = expf(scale_t(p.target[(int64_t)(b * p.Tr + lane) * p.V + tok], T) - Mt) * it;
-        const float ratio = q_tok > 0.f ? fminf(__fdiv_rn(p_tok, fmaxf(q_tok, 1e-10f)), 1.0f) : 0.f;
-        acc = accept_uniform(p, b, lane) < ratio;
-        p.out_mask[b * p.k + lane] = acc ? 1 : 0;
-    }
-    const unsigned bal = __ballot_sync(0xffffffffu, acc);
-    const unsigned low = p.k >= 32 ? 0xffffffffu : ((1u << p.k) - 1u);
-    const unsigned rej = ~bal & low;
-    const int a = rej ? __ffs(rej) - 1 : p.k;
-    float Mp = 0.f, ip = 0.f, Mq = 0.f, iq = 0.f;
-    if (lane == 0) row_norm(p, nd + b * p.Tr + min(a, p.Tr - 1), Mp, ip);  // verify.py:143
-    if (lane == 1 && a < p.k && !p.point_mass) row_norm(p, b * p.k + a, Mq, iq);
-    Mq = __shfl_sync(0xffffffffu, Mq, 1);
-    iq = __shfl_sync(0xffffffffu, iq, 1);
-    if (lane == 0) {
-        Decision d;
-        d.a = a;
-        d.mask = bal & low;
-        d.Mp = Mp;
-        d.ip = ip;
-        d.Mq = Mq;
-        d.iq = iq;
-        *out = d;
-        p.out_acc[b] = a;
-    }
-}
-
 // ------------------------------------------------------------------ pass 1
-__global__ void __launch_bounds__(THREADS) vs_row_stats(const Params p) {
+// Sum of exp(x - max) by the hardware base-2 exponential: relative error ~2^-22 per
+// term, far below what the decisions can resolve (they compare against uniforms).
+__global__ void __launch_bounds__(THREADS, 4) vs_row_stats(const Params p) {
     __shared__ float sh[THREADS / 32];
-    __shared__ int last;
     const int nd = p.B * p.k;
     // point-mass drafts need no statistics: the grid then starts at the target rows
     const int row = blockIdx.x + (p.point_mass ? nd : 0);
@@ -244,17 +179,21 @@ __global__ void __launch_bounds__(THREADS) vs_row_stats(const Params p) {
             const int idx = it * THREADS * 4 + threadIdx.x * 4;
             float4 x = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
             if (idx < n) x = __ldcs(reinterpret_cast<const float4*>(src + base + idx));
-            v[it * 4 + 0] = idx < n ? scale_t(x.x, T) : -INFINITY;
-            v[it * 4 + 1] = idx < n ? scale_t(x.y, T) : -INFINITY;
-            v[it * 4 + 2] = idx < n ? scale_t(x.z, T) : -INFINITY;
-            v[it * 4 + 3] = idx < n ? scale_t(x.w, T) : -INFINITY;
+            v[it * 4 + 0] = idx < n ? x.x : -INFINITY;
+            v[it * 4 + 1] = idx < n ? x.y : -INFINITY;
+            v[it * 4 + 2] = idx < n ? x.z : -INFINITY;
+            v[it * 4 + 3] = idx < n ? x.w : -INFINITY;
         }
     } else {
 #pragma unroll
         for (int it = 0; it < EPT; ++it) {
             const int idx = it * THREADS + threadIdx.x;
-            v[it] = idx < n ? scale_t(__ldcs(src + base + idx), T) : -INFINITY;
+            v[it] = idx < n ? __ldcs(src + base + idx) : -INFINITY;
         }
+    }
+    if (T != 1.0f) {  // x / T as torch divides (IEEE), one uniform branch per CTA
+#pragma unroll
+        for (int i = 0; i < EPT; ++i) v[i] = __fdiv_rn(v[i], T);
     }
     float mx = -INFINITY;
 #pragma unroll
@@ -262,35 +201,221 @@ __global__ void __launch_bounds__(THREADS) vs_row_stats(const Params p) {
     mx = block_reduce(mx, [](float a, float b2) { return fmaxf(a, b2); }, sh);
     float s = 0.f;
     if (mx != -INFINITY) {
+        constexpr float kLog2e = 1.4426950408889634f;
+        const float off = -mx * kLog2e;
 #pragma unroll
-        for (int i = 0; i < EPT; ++i) s += expf(v[i] - mx);
+        for (int i = 0; i < EPT; ++i) s += ex2(fmaf(v[i], kLog2e, off));
     }
     s = block_reduce(s, [](float a, float b2) { return a + b2; }, sh);
+    if (threadIdx.x < SUB)
+        __stcg(p.stats + ((int64_t)row * p.C1 + c) * SUB + threadIdx.x,
+               threadIdx.x == 0 ? make_float2(mx, s) : make_float2(-INFINITY, 0.f));
+}
+
+// Pass 1 for 16-byte-aligned rows with V % 4 == 0: items (row, chunk) strided over
+// persistent CTAs; the last warp streams each item's 32 KB into the stage ring with one
+// bulk copy, the consumer warps reduce it from shared memory and release the stage.
+SDB_DEV const float* logits_row(const Params& p, int row, int& b) {
+    const int nd = p.B * p.k;
+    if (row < nd) {
+        b = row / p.k;
+        return p.draft + (int64_t)row * p.V;
+    }
+    b = (row - nd) / p.Tr;
+    return p.target + (int64_t)(row - nd) * p.V;
+}
+
+__global__ void __launch_bounds__(BS_THREADS, 2) vs_row_stats_bulk(const Params p, int row0, int nrows) {
+    extern __shared__ __align__(128) uint8_t ring[];
+    __shared__ __align__(8) uint64_t bars[2 * BS_STAGES];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int total = nrows * p.C1;
+    const uint32_t full0 = smem_u32(bars), empty0 = full0 + 8 * BS_STAGES;
     if (threadIdx.x == 0) {
-        __stcg(p.stats + (int64_t)row * p.C1 + c, make_float2(mx, s));
-        __threadfence();
-        const int expect = (p.point_mass ? p.Tr : p.k + p.Tr) * p.C1;
-        last = atomicAdd(p.counters + b, 1) == expect - 1;
+        for (int s = 0; s < BS_STAGES; ++s) {
+            mbar_init(full0 + 8 * s, 1);
+            mbar_init(empty0 + 8 * s, BS_CONSUMERS);
+        }
+        fence_mbarrier_init();
     }
     __syncthreads();
-    if (!last) return;
-    // last statistics CTA of sequence b: decide once for the whole sequence
-    __threadfence();
-    if (threadIdx.x < 32) {
-        decide_warp(p, b, p.dec + b);
-        if (threadIdx.x == 0) p.counters[b] = 0;
+    if (warp == BS_CONSUMERS) {
+        if (lane == 0) {
+            const uint64_t pol = l2_policy_evict_first();
+            int g = 0;
+            for (int it = blockIdx.x; it < total; it += gridDim.x, ++g) {
+                const int s = g % BS_STAGES;
+                if (g >= BS_STAGES && !mbar_wait_sleep(empty0 + 8 * s, ((g / BS_STAGES) - 1) & 1)) {
+                    atomicOr(p.err, SDB_KERR_TIMEOUT);
+                    break;
+                }
+                int b;
+                const int c = it % p.C1;
+                const float* src = logits_row(p, row0 + it / p.C1, b) + c * CHUNK1;
+                const uint32_t bytes = 4u * (uint32_t)min(CHUNK1, p.V - c * CHUNK1);
+                mbar_arrive_expect_tx(full0 + 8 * s, bytes);
+                bulk_load(smem_u32(ring + s * CHUNK1 * 4), src, bytes, full0 + 8 * s, pol);
+            }
+            for (int q = g - BS_STAGES > 0 ? g - BS_STAGES : 0; q < g; ++q)  // own copies land before exit
+                if (!mbar_wait(full0 + 8 * (q % BS_STAGES), (q / BS_STAGES) & 1)) break;
+        }
+        return;
+    }
+    // consumer warp w reduces logits [512 w, 512 w + 512) of each chunk on its own
+    bool ok = true;
+    int g = 0;
+    for (int it = blockIdx.x; it < total; it += gridDim.x, ++g) {
+        const int s = g % BS_STAGES;
+        if (ok && !mbar_wait_sleep(full0 + 8 * s, (g / BS_STAGES) & 1)) {
+            ok = false;
+            if (lane == 0) atomicOr(p.err, SDB_KERR_TIMEOUT);
+        }
+        int b;
+        const int row = row0 + it / p.C1, c = it % p.C1;
+        logits_row(p, row, b);
+        const float T = p.temps ? p.temps[b] : 1.0f;
+        const int n = min(CHUNK1, p.V - c * CHUNK1);
+        const float4* st = reinterpret_cast<const float4*>(ring + s * CHUNK1 * 4) + warp * (CHUNK1 / 4 / SUB);
+        float v[BS_EPT];
+        if (n == CHUNK1) {
+#pragma unroll
+            for (int q = 0; q < BS_EPT / 4; ++q) {
+                const float4 x = st[q * 32 + lane];
+                v[4 * q + 0] = x.x;
+                v[4 * q + 1] = x.y;
+                v[4 * q + 2] = x.z;
+                v[4 * q + 3] = x.w;
+            }
+        } else {  // the last chunk of a row
+#pragma unroll
+            for (int q = 0; q < BS_EPT / 4; ++q) {
+                const int i4 = q * 32 + lane;
+                const float4 x = st[i4];
+                const bool in = 4 * (warp * (CHUNK1 / 4 / SUB) + i4) < n;
+                v[4 * q + 0] = in ? x.x : -INFINITY;
+                v[4 * q + 1] = in ? x.y : -INFINITY;
+                v[4 * q + 2] = in ? x.z : -INFINITY;
+                v[4 * q + 3] = in ? x.w : -INFINITY;
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty0 + 8 * s);
+        if (T != 1.0f) {  // x / T as torch divides (IEEE); -inf / T stays -inf
+#pragma unroll
+            for (int i = 0; i < BS_EPT; ++i) v[i] = __fdiv_rn(v[i], T);
+        }
+        float m4[4] = {v[0], v[1], v[2], v[3]};
+#pragma unroll
+        for (int i = 4; i < BS_EPT; ++i) m4[i & 3] = fmaxf(m4[i & 3], v[i]);
+        float mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        float sum = 0.f;
+        if (mx != -INFINITY) {
+            constexpr float kLog2e = 1.4426950408889634f;
+            const float off = -mx * kLog2e;
+            float s4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int i = 0; i < BS_EPT; ++i) s4[i & 3] += ex2(fmaf(v[i], kLog2e, off));
+            sum = (s4[0] + s4[1]) + (s4[2] + s4[3]);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        if (lane == 0) __stcg(p.stats + ((int64_t)row * p.C1 + c) * SUB + warp, make_float2(mx, sum));
+    }
+}
+
+// ------------------------------------------------------------------ pass 2
+// One CTA per sequence: warp w merges the chunk statistics of rows w, w + 16, ...
+// (the k draft rows, then the target rows) into (max, 1/sum); warp 0 then makes the
+// k acceptance decisions, one candidate per lane:
+// ratio = where(q_tok > 0, min(p_tok / max(q_tok, 1e-10), 1), 0); accept = u < ratio
+// (verify.py:109-121); accepted = first rejection or k (:125-129).
+constexpr int DECIDE_THREADS = 512;
+__global__ void __launch_bounds__(DECIDE_THREADS) vs_decide(const Params p) {
+    __shared__ float sM[65], sI[65];
+    const int b = blockIdx.x;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nd = p.B * p.k;
+    const int nrows = p.k + p.Tr;
+    for (int r = warp; r < nrows; r += DECIDE_THREADS / 32) {
+        if (r < p.k && p.point_mass) continue;
+        const int grow = r < p.k ? b * p.k + r : nd + b * p.Tr + (r - p.k);
+        const float2* st = p.stats + (int64_t)grow * p.C1 * SUB;
+        const int np = p.C1 * SUB;
+        constexpr int kHeld = 16;  // partials per lane kept in registers (V up to 2^22)
+        float2 h[kHeld];
+        float M = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < kHeld; ++j) {
+            const int c = lane + 32 * j;
+            h[j] = c < np ? __ldcg(st + c) : make_float2(-INFINITY, 0.f);
+            M = fmaxf(M, h[j].x);
+        }
+        for (int c = lane + 32 * kHeld; c < np; c += 32) M = fmaxf(M, __ldcg(st + c).x);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+        float S = 0.f;
+#pragma unroll
+        for (int j = 0; j < kHeld; ++j)
+            if (h[j].x != -INFINITY) S += h[j].y * expf(h[j].x - M);
+        for (int c = lane + 32 * kHeld; c < np; c += 32) {
+            const float2 v = __ldcg(st + c);
+            if (v.x != -INFINITY) S += v.y * expf(v.x - M);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) S += __shfl_xor_sync(0xffffffffu, S, o);
+        if (lane == 0) {
+            sM[r] = M;
+            sI[r] = 1.0f / S;
+        }
+    }
+    __syncthreads();
+    if (warp != 0) return;
+    const float T = p.temps ? p.temps[b] : 1.0f;
+    bool acc = true;
+    if (lane < p.k) {
+        int64_t tok = p.tokens[b * p.k + lane];
+        if (tok < 0 || tok >= p.V) {
+            atomicOr(p.err, SDB_KERR_TOKEN);
+            tok = 0;
+        }
+        const int drow = b * p.k + lane;
+        const float xq = p.draft[(int64_t)drow * p.V + tok];
+        const float q_tok = p.point_mass ? xq : expf(scale_t(xq, T) - sM[lane]) * sI[lane];
+        const float p_tok =
+            expf(scale_t(p.target[(int64_t)(b * p.Tr + lane) * p.V + tok], T) - sM[p.k + lane]) * sI[p.k + lane];
+        const float ratio = q_tok > 0.f ? fminf(__fdiv_rn(p_tok, fmaxf(q_tok, 1e-10f)), 1.0f) : 0.f;
+        acc = accept_uniform(p, b, lane) < ratio;
+        p.out_mask[b * p.k + lane] = acc ? 1 : 0;
+    }
+    const unsigned bal = __ballot_sync(0xffffffffu, acc);
+    const unsigned low = p.k >= 32 ? 0xffffffffu : ((1u << p.k) - 1u);
+    const unsigned rej = ~bal & low;
+    const int a = rej ? __ffs(rej) - 1 : p.k;
+    if (lane == 0) {
+        Decision d;
+        d.a = a;
+        d.mask = bal & low;
+        const int tr = p.k + min(a, p.Tr - 1);  // verify.py:143
+        d.Mp = sM[tr];
+        d.ip = sI[tr];
+        const bool hq = a < p.k && !p.point_mass;
+        d.Mq = hq ? sM[a] : 0.f;
+        d.iq = hq ? sI[a] : 0.f;
+        p.dec[b] = d;
+        p.out_acc[b] = a;
     }
 }
 
 // resid_i and p_i of row a (verify.py:141-148): q_pad[k] = 0, p index clamped.
-SDB_DEV void resid_at(const Params& p, int b, const Decision& d, float T, int i, float& r, float& pv) {
-    const int pa = min(d.a, p.Tr - 1);
-    pv = expf(scale_t(__ldg(p.target + (int64_t)(b * p.Tr + pa) * p.V + i), T) - d.Mp) * d.ip;
+// UNIT: temperature 1 (x / T is x); the callers branch once per CTA so no division
+// is evaluated for the common case.
+template <bool UNIT>
+SDB_DEV void resid_of(const Params& p, const Decision& d, float T, float xt, float xd, float& r, float& pv) {
+    pv = expf((UNIT ? xt : __fdiv_rn(xt, T)) - d.Mp) * d.ip;
     float qv = 0.f;
-    if (d.a < p.k) {
-        const float x = __ldg(p.draft + (int64_t)(b * p.k + d.a) * p.V + i);
-        qv = p.point_mass ? x : expf(scale_t(x, T) - d.Mq) * d.iq;
-    }
+    if (d.a < p.k) qv = p.point_mass ? xd : expf((UNIT ? xd : __fdiv_rn(xd, T)) - d.Mq) * d.iq;
     r = fmaxf(pv - qv, 0.f);
 }
 
@@ -303,21 +428,70 @@ SDB_DEV Decision load_decision(const Params& p, int b) {
     return d;
 }
 
-// ------------------------------------------------------------------ pass 2
+// Row a of the target (clamped) and of the draft (none when a == k) for sequence b.
+SDB_DEV const float* target_row_a(const Params& p, int b, const Decision& d) {
+    return p.target + (int64_t)(b * p.Tr + min(d.a, p.Tr - 1)) * p.V;
+}
+SDB_DEV const float* draft_row_a(const Params& p, int b, const Decision& d) {
+    return d.a < p.k ? p.draft + (int64_t)(b * p.k + d.a) * p.V : nullptr;
+}
+
+// Visits the logits of this CTA's chunk of row a as (index, target logit, draft
+// logit): float4 loads issued together when V % 4 == 0, scalar loads otherwise.
+template <typename F>
+SDB_DEV void for_chunk(const Params& p, const float* tr, const float* dr, int base, F f) {
+    const int n = min(CHUNK2, p.V - base);
+    if ((p.V & 3) == 0) {
+        float4 xt[EPT2 / 4], xd[EPT2 / 4];
+#pragma unroll
+        for (int it = 0; it < EPT2 / 4; ++it) {
+            const int idx = it * THREADS * 4 + threadIdx.x * 4;
+            xt[it] = make_float4(0.f, 0.f, 0.f, 0.f);
+            xd[it] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (idx < n) {
+                xt[it] = __ldg(reinterpret_cast<const float4*>(tr + base + idx));
+                if (dr) xd[it] = __ldg(reinterpret_cast<const float4*>(dr + base + idx));
+            }
+        }
+#pragma unroll
+        for (int it = 0; it < EPT2 / 4; ++it) {
+            const int idx = it * THREADS * 4 + threadIdx.x * 4;
+            if (idx < n) f(base + idx, xt[it], xd[it]);
+        }
+    } else {
+        for (int idx = threadIdx.x; idx < n; idx += THREADS) {
+            const float4 t1 = make_float4(__ldg(tr + base + idx), 0.f, 0.f, 0.f);
+            const float4 d1 = make_float4(dr ? __ldg(dr + base + idx) : 0.f, 0.f, 0.f, 0.f);
+            f(base + idx, t1, d1);  // only .x is meaningful: lanes of one logit
+        }
+    }
+}
+
+// ------------------------------------------------------------------ pass 3
 __global__ void __launch_bounds__(THREADS) vs_resid_sums(const Params p) {
     __shared__ float sh[THREADS / 32];
     const int b = blockIdx.x, c = blockIdx.y;
     const Decision d = load_decision(p, b);
     const float T = p.temps ? p.temps[b] : 1.0f;
+    const float* tr = target_row_a(p, b, d);
+    const float* dr = draft_row_a(p, b, d);
+    const int cnt = (p.V & 3) == 0 ? 4 : 1;
     float sr = 0.f, sp = 0.f;
-    const int base = c * CHUNK2;
-    const int end = min(base + CHUNK2, p.V);
-    for (int i = base + threadIdx.x; i < end; i += THREADS) {
-        float r, pv;
-        resid_at(p, b, d, T, i, r, pv);
-        sr += r;
-        sp += pv;
-    }
+    auto body = [&](auto unit) {
+        for_chunk(p, tr, dr, c * CHUNK2, [&](int, const float4& xt, const float4& xd) {
+            const float t4[4] = {xt.x, xt.y, xt.z, xt.w}, d4[4] = {xd.x, xd.y, xd.z, xd.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+                if (e < cnt) {
+                    float r, pv;
+                    resid_of<decltype(unit)::value>(p, d, T, t4[e], d4[e], r, pv);
+                    sr += r;
+                    sp += pv;
+                }
+        });
+    };
+    if (T == 1.0f) body(std::true_type{});
+    else body(std::false_type{});
     sr = block_reduce(sr, [](float a, float b2) { return a + b2; }, sh);
     sp = block_reduce(sp, [](float a, float b2) { return a + b2; }, sh);
     if (threadIdx.x == 0) __stcg(p.rsum + b * p.C2 + c, make_float2(sr, sp));
@@ -325,7 +499,25 @@ __global__ void __launch_bounds__(THREADS) vs_resid_sums(const Params p) {
 
 SDB_DEV bool better(float v, int i, float bv, int bi) { return v > bv || (v == bv && i < bi); }
 
-// ------------------------------------------------------------------ pass 3
+// max(E, 1e-10) for columns i .. i + cnt - 1 of sequence b (cnt = 4: i % 4 == 0, one
+// Philox block gives the four words).
+SDB_DEV void exp_noise4(const Params& p, int b, int i, int cnt, float (&E)[4]) {
+    if (p.e) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) E[e] = e < cnt ? p.e[(int64_t)b * p.V + i + e] : 1.f;
+    } else if (cnt == 4) {
+        uint32_t c[4] = {(uint32_t)i >> 2, (uint32_t)b, 1u, p.offset};
+        philox(c, p.seed_lo, p.seed_hi);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) E[e] = -log_fixed(word_to_open_uniform(c[e]));
+    } else {
+        E[0] = -log_fixed(word_to_open_uniform(philox_word(p.seed_lo, p.seed_hi, p.offset, 1u, (uint32_t)b, (uint32_t)i)));
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) E[e] = fmaxf(E[e], 1e-10f);  // clamp_min_(1e-10), verify.py:209
+}
+
+// ------------------------------------------------------------------ pass 4
 __global__ void __launch_bounds__(THREADS) vs_bonus(const Params p) {
     __shared__ float zsh;
     __shared__ int use_p;
@@ -333,34 +525,137 @@ __global__ void __launch_bounds__(THREADS) vs_bonus(const Params p) {
     __shared__ int bi[THREADS / 32];
     const int b = blockIdx.x, c = blockIdx.y;
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    if (threadIdx.x == 0) {
+    if (threadIdx.x < 32) {  // the chunk sums of pass 3, loaded by all lanes at once
         float sr = 0.f, sp = 0.f;
-        for (int cc = 0; cc < p.C2; ++cc) {
+        for (int cc = lane; cc < p.C2; cc += 32) {
             const float2 v = __ldcg(p.rsum + b * p.C2 + cc);
             sr += v.x;
             sp += v.y;
         }
-        use_p = !(sr > 0.f);                   // fallback to p[a], verify.py:151
-        zsh = fmaxf(use_p ? sp : sr, 1e-10f);  // normaliser, verify.py:152
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            sr += __shfl_xor_sync(0xffffffffu, sr, o);
+            sp += __shfl_xor_sync(0xffffffffu, sp, o);
+        }
+        if (lane == 0) {
+            use_p = !(sr > 0.f);                   // fallback to p[a], verify.py:151
+            zsh = fmaxf(use_p ? sp : sr, 1e-10f);  // normaliser, verify.py:152
+        }
     }
     __syncthreads();
     const Decision d = load_decision(p, b);
     const float T = p.temps ? p.temps[b] : 1.0f;
     const float Z = zsh;
     const bool up = use_p != 0;
+    const float* tr = target_row_a(p, b, d);
+    const float* dr = draft_row_a(p, b, d);
+    const int cnt = (p.V & 3) == 0 ? 4 : 1;
     float best = -INFINITY;
     int bidx = 0x7fffffff;
-    const int base = c * CHUNK2;
-    const int end = min(base + CHUNK2, p.V);
-    for (int i = base + threadIdx.x; i < end; i += THREADS) {
+    // Exact value of column i: (v / Z) / max(E, 1e-10) with v = p[a] or resid[a].
+    auto exact = [&](auto unit, int i, float xt, float xd, float E) {
         float r, pv;
-        resid_at(p, b, d, T, i, r, pv);
-        const float x = __fdiv_rn(__fdiv_rn(up ? pv : r, Z), exp_noise(p, b, i));
+        resid_of<decltype(unit)::value>(p, d, T, xt, xd, r, pv);
+        const float v = up ? pv : r;
+        const float x = v != 0.f ? __fdiv_rn(__fdiv_rn(v, Z), E) : 0.f;  // 0 / Z / E is +0
         if (better(x, i, best, bidx)) {
             best = x;
             bidx = i;
         }
-    }
+    };
+    auto body = [&](auto unit) {
+        if ((p.V & 3) != 0) {
+            for_chunk(p, tr, dr, c * CHUNK2, [&](int i, const float4& xt, const float4& xd) {
+                float E[4];
+                exp_noise4(p, b, i, 1, E);
+                exact(unit, i, xt.x, xd.x, E[0]);
+            });
+            return;
+        }
+        // V % 4 == 0: every lane holds 16 columns (4 runs of 4).  Cheap bounds first:
+        // v in [v_lo, v_hi] from fast exponentials (within 2^-10 of expf above
+        // exponent -8192; the residual max(p - q, 0) from p_lo - q_hi and p_hi) and
+        // E = max(-log U, 1e-10) in [max(1 - U, 1e-10), max((1 - U) / U, 1e-10)].  The
+        // warp's largest v_lo / E_hi is a lower bound of its best value; only columns
+        // whose v_hi / E_lo reaches it are evaluated exactly, and the others are
+        // strictly below an evaluated one, so the argmax (first index on ties) is the
+        // one of the exact values.  The winner has U near 1, where the E bounds meet.
+        const int base = c * CHUNK2;
+        const int n = min(CHUNK2, p.V - base);
+        float4 xt[EPT2 / 4], xd[EPT2 / 4];
+#pragma unroll
+        for (int q = 0; q < EPT2 / 4; ++q) {
+            const int idx = q * THREADS * 4 + threadIdx.x * 4;
+            xt[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+            xd[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (idx < n) {
+                xt[q] = __ldg(reinterpret_cast<const float4*>(tr + base + idx));
+                if (dr) xd[q] = __ldg(reinterpret_cast<const float4*>(dr + base + idx));
+            }
+        }
+        constexpr float kLog2e = 1.4426950408889634f;
+        const bool has_q = d.a < p.k;
+        float vhi[EPT2], elo[EPT2];
+        float lbmax = 0.f;
+#pragma unroll
+        for (int q = 0; q < EPT2 / 4; ++q) {
+            const int idx = q * THREADS * 4 + threadIdx.x * 4;
+            const bool in = idx < n;
+            const float t4[4] = {xt[q].x, xt[q].y, xt[q].z, xt[q].w};
+            const float d4[4] = {xd[q].x, xd[q].y, xd[q].z, xd[q].w};
+            uint32_t w4[4] = {(uint32_t)(base + idx) >> 2, (uint32_t)b, 1u, p.offset};
+            if (!p.e && in) philox(w4, p.seed_lo, p.seed_hi);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int j = 4 * q + e;
+                float Elo, Ehi;
+                if (p.e) {
+                    Elo = Ehi = in ? fmaxf(p.e[(int64_t)b * p.V + base + idx + e], 1e-10f) : 1.f;
+                } else {
+                    // -log U in [1 - U, (1 - U)(3 - 2U)] for U >= 1/2 and <= 17 always
+                    // (U >= 2^-24); 1 - U is exact (U is a multiple of 2^-24); the factors
+                    // cover the few ulps by which log_fixed may sit on either side
+                    const float U = word_to_open_uniform(w4[e]);
+                    Elo = fmaxf((1.0f - U) * 0.99999f, 1e-10f);
+                    Ehi = U >= 0.5f ? fmaxf((1.0f - U) * (3.0f - 2.0f * U) * 1.00002f, 1e-10f) : 17.0f;
+                }
+                const float xs = decltype(unit)::value ? t4[e] : __fdiv_rn(t4[e], T);
+                const float pf = ex2((xs - d.Mp) * kLog2e) * d.ip;
+                float hi = fmaxf(pf * 1.001f, FLT_MIN);
+                float lo = pf * 0.999f;
+                if (!up && has_q) {
+                    const float xq = decltype(unit)::value || p.point_mass ? d4[e] : __fdiv_rn(d4[e], T);
+                    const float qf = p.point_mass ? xq : ex2((xq - d.Mq) * kLog2e) * d.iq;
+                    lo = fmaxf(lo - fmaxf(qf * 1.001f, FLT_MIN), 0.f);
+                    if (p.point_mass) hi += fmaxf(-qf, 0.f) * 1.001f;  // a negative draft value raises r
+                }
+                vhi[j] = in ? hi : -1.f;
+                elo[j] = Elo;
+                if (in) lbmax = fmaxf(lbmax, __fdividef(lo, Ehi) * 0.9999f);
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) lbmax = fmaxf(lbmax, __shfl_xor_sync(0xffffffffu, lbmax, o));
+        const float thr = lbmax * 0.9999f;  // slack for the rounding of these bounds
+        uint32_t live = 0;  // columns whose v_hi / E_lo reaches the threshold
+#pragma unroll
+        for (int j = 0; j < EPT2; ++j)
+            if (vhi[j] >= 0.f && !(vhi[j] < thr * elo[j])) live |= 1u << j;
+        // the exact evaluation exists once in the code (not per unrolled column): the
+        // few live columns reload their two logits from cache
+        while (live) {
+            const int j = __ffs(live) - 1;
+            live &= live - 1;
+            const int i = base + (j >> 2) * THREADS * 4 + threadIdx.x * 4 + (j & 3);
+            const float E = p.e ? fmaxf(p.e[(int64_t)b * p.V + i], 1e-10f)
+                                : fmaxf(-log_fixed(word_to_open_uniform(philox_word(
+                                            p.seed_lo, p.seed_hi, p.offset, 1u, (uint32_t)b, (uint32_t)i))),
+                                        1e-10f);
+            exact(unit, i, __ldg(tr + i), dr ? __ldg(dr + i) : 0.f, E);
+        }
+    };
+    if (T == 1.0f) body(std::true_type{});
+    else body(std::false_type{});
 #pragma unroll
     for (int s = 16; s > 0; s >>= 1) {
         const float ov = __shfl_xor_sync(0xffffffffu, best, s);
@@ -375,20 +670,25 @@ __global__ void __launch_bounds__(THREADS) vs_bonus(const Params p) {
         bi[w] = bidx;
     }
     __syncthreads();
-    if (threadIdx.x != 0) return;
-    for (int i = 1; i < THREADS / 32; ++i)
-        if (better(bv[i], bi[i], best, bidx)) {
-            best = bv[i];
-            bidx = bi[i];
-        }
-    __stcg(p.amax + b * p.C2 + c, make_float2(best, __int_as_float(bidx)));
-    __threadfence();
-    if (atomicAdd(p.counters + b, 1) != p.C2 - 1) return;
+    if (threadIdx.x >= 32) return;
+    __shared__ int last;
+    if (lane == 0) {
+        for (int i = 1; i < THREADS / 32; ++i)
+            if (better(bv[i], bi[i], best, bidx)) {
+                best = bv[i];
+                bidx = bi[i];
+            }
+        __stcg(p.amax + b * p.C2 + c, make_float2(best, __int_as_float(bidx)));
+        __threadfence();
+        last = atomicAdd(p.counters + b, 1) == p.C2 - 1;
+    }
+    __syncwarp();
+    if (!last) return;
     // last CTA of sequence b: finish the argmax (first index on ties, torch.argmax)
     __threadfence();
     float gb = -INFINITY;
     int gi = 0x7fffffff;
-    for (int cc = 0; cc < p.C2; ++cc) {
+    for (int cc = lane; cc < p.C2; cc += 32) {
         const float2 v = __ldcg(p.amax + b * p.C2 + cc);
         const int vi = __float_as_int(v.y);
         if (better(v.x, vi, gb, gi)) {
@@ -396,8 +696,19 @@ __global__ void __launch_bounds__(THREADS) vs_bonus(const Params p) {
             gi = vi;
         }
     }
-    p.out_bonus[b] = gi == 0x7fffffff ? 0 : gi;
-    p.counters[b] = 0;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, gb, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, gi, o);
+        if (better(ov, oi, gb, gi)) {
+            gb = ov;
+            gi = oi;
+        }
+    }
+    if (lane == 0) {
+        p.out_bonus[b] = gi == 0x7fffffff ? 0 : gi;
+        p.counters[b] = 0;
+    }
 }
 
 struct WsLayout {
@@ -418,7 +729,7 @@ static WsLayout ws_layout(int B, int k, int Tr, int V) {
     w.dec = off;
     off = align_up(off + sizeof(Decision) * B, 256);
     w.stats = off;
-    off = align_up(off + sizeof(float2) * (size_t)B * (k + Tr) * C1, 256);
+    off = align_up(off + sizeof(float2) * (size_t)B * (k + Tr) * C1 * SUB, 256);
     w.rsum = off;
     off = align_up(off + sizeof(float2) * (size_t)B * C2, 256);
     w.amax = off;
@@ -498,8 +809,24 @@ extern "C" int sdb_verify_batch(const float* draft, const float* target, const i
     p.rsum = reinterpret_cast<float2*>(ws + w.rsum);
     p.amax = reinterpret_cast<float2*>(ws + w.amax);
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    vs::vs_row_stats<<<dim3(B * ((point_mass ? 0 : k) + Tr), p.C1), vs::THREADS, 0, st>>>(p);
-    int rc = cuda_status(cudaGetLastError(), "vs_row_stats launch");
+    const int row0 = point_mass ? B * k : 0;
+    const int nrows = B * ((point_mass ? 0 : k) + Tr);
+    int rc;
+    if ((V & 3) == 0) {  // rows 16-byte aligned (the pointers were checked above)
+        rc = ensure_smem_attr(reinterpret_cast<const void*>(vs::vs_row_stats_bulk), vs::BS_SMEM, 50);
+        if (rc) return rc;
+        const long long items = (long long)nrows * p.C1;
+        const int slots = 2 * device_sm_count();
+        const int grid = (int)(items < slots ? items : slots);
+        vs::vs_row_stats_bulk<<<grid, vs::BS_THREADS, vs::BS_SMEM, st>>>(p, row0, nrows);
+        rc = cuda_status(cudaGetLastError(), "vs_row_stats_bulk launch");
+    } else {
+        vs::vs_row_stats<<<dim3(nrows, p.C1), vs::THREADS, 0, st>>>(p);
+        rc = cuda_status(cudaGetLastError(), "vs_row_stats launch");
+    }
+    if (rc) return rc;
+    vs::vs_decide<<<B, vs::DECIDE_THREADS, 0, st>>>(p);
+    rc = cuda_status(cudaGetLastError(), "vs_decide launch");
     if (rc) return rc;
     vs::vs_resid_sums<<<dim3(B, p.C2), vs::THREADS, 0, st>>>(p);
     rc = cuda_status(cudaGetLastError(), "vs_resid_sums launch");
