@@ -113,6 +113,15 @@ SDB_DEV void tma_load_4d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int
         : "memory");
 }
 
+// 2-D tiled TMA load into this CTA's shared memory, completing on an mbarrier.
+SDB_DEV void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int c0, int c1, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+        " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "l"(policy)
+        : "memory");
+}
+
 // Contiguous bulk copy global -> this CTA's shared memory, completing on an mbarrier
 // (both addresses 16-byte aligned, bytes a multiple of 16).  No multicast.
 SDB_DEV void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar, uint64_t policy) {

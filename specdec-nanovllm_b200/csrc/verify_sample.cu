@@ -549,7 +549,6 @@ __global__ void __launch_bounds__(THREADS) vs_bonus(const Params p) {
     const bool up = use_p != 0;
     const float* tr = target_row_a(p, b, d);
     const float* dr = draft_row_a(p, b, d);
-    const int cnt = (p.V & 3) == 0 ? 4 : 1;
     float best = -INFINITY;
     int bidx = 0x7fffffff;
     // Exact value of column i: (v / Z) / max(E, 1e-10) with v = p[a] or resid[a].

@@ -276,11 +276,23 @@ struct WsLayout {
     size_t counters, part, total;
 };
 
+}  // namespace w8
+
+bool w8a16_stream_eligible(int M, int N, int K, int group);
+size_t w8a16_stream_partial_bytes(int M, int N, int K);
+int w8a16_stream_launch(const void* x, int64_t x_srow, const int8_t* w, const void* s, int s_dtype, const void* bias,
+                        void* y, int64_t y_srow, int M, int N, int K, int act_dtype, int* counters, float* part,
+                        int* err, cudaStream_t st);
+
+namespace w8 {
+
 // Split-K counters at a fixed offset with a fixed capacity: one workspace serves
 // calls of any shape in any order (counters are never aliased by partials and
 // every call leaves them at 0).
 constexpr int kCounterCap = 65536;  // output tiles
 
+// Both paths share the counter region at offset 0; the streaming path keeps an error
+// word right after it and its partials after that.
 static WsLayout ws_layout(int M, int N, int K) {
     Plan pl = plan(M, N, K);
     WsLayout w;
@@ -290,6 +302,13 @@ static WsLayout ws_layout(int M, int N, int K) {
     if (pl.SK > 1) off = align_up(off + sizeof(float) * (size_t)pl.SK * M * N, 256);
     w.total = off;
     return w;
+}
+
+constexpr size_t kStreamErrOffset = 256 * 1024;            // == align_up(4 * kCounterCap, 256)
+constexpr size_t kStreamPartOffset = kStreamErrOffset + 256;
+
+static size_t stream_ws_bytes(int M, int N, int K) {
+    return align_up(kStreamPartOffset + w8a16_stream_partial_bytes(M, N, K), 256);
 }
 
 template <typename T>
@@ -317,7 +336,12 @@ using namespace sdb;
 
 extern "C" size_t sdb_w8a16_workspace_size(int M, int N, int K) {
     if (M <= 0 || N <= 0 || K <= 0 || K % w8::KC) return 256;
-    return w8::ws_layout(M, N, K).total;
+    size_t total = w8::ws_layout(M, N, K).total;
+    if (w8a16_stream_eligible(M, N, K, 0)) {
+        const size_t s = w8::stream_ws_bytes(M, N, K);
+        if (s > total) total = s;
+    }
+    return total;
 }
 
 extern "C" int sdb_w8a16_linear(const void* x, int64_t x_srow, const int8_t* qweight, const void* scale,
@@ -348,6 +372,18 @@ extern "C" int sdb_w8a16_linear(const void* x, int64_t x_srow, const int8_t* qwe
         set_last_error("x and qweight must be 16-byte aligned with x row stride %% 8 == 0; workspace 256-aligned");
         return SDB_ERR_INVALID_ARG;
     }
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (w8a16_stream_eligible(M, N, K, group_size)) {
+        const size_t need = w8::stream_ws_bytes(M, N, K);
+        if (workspace_bytes < need) {
+            set_last_error("workspace too small: need %zu bytes, got %zu", need, workspace_bytes);
+            return SDB_ERR_WORKSPACE;
+        }
+        uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
+        return w8a16_stream_launch(x, x_srow, qweight, scale, scale_dtype, bias, y, y_srow, M, N, K, act_dtype,
+                                   reinterpret_cast<int*>(ws), reinterpret_cast<float*>(ws + w8::kStreamPartOffset),
+                                   reinterpret_cast<int*>(ws + w8::kStreamErrOffset), st);
+    }
     w8::WsLayout wl = w8::ws_layout(M, N, K);
     if (workspace_bytes < wl.total) {
         set_last_error("workspace too small: need %zu bytes, got %zu", wl.total, workspace_bytes);
@@ -375,7 +411,6 @@ extern "C" int sdb_w8a16_linear(const void* x, int64_t x_srow, const int8_t* qwe
     p.chunks_per_split = pl.cps;
     p.counters = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(workspace) + wl.counters);
     p.part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) + wl.part);
-    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     if (act_dtype == SDB_BF16) return w8::launch<__nv_bfloat16>(p, pl, st, group_size != 0);
     return w8::launch<__half>(p, pl, st, group_size != 0);
 }
