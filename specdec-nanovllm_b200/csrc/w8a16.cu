@@ -17,6 +17,8 @@
 // the caller's workspace and the last CTA of an output tile (atomic counter,
 // reset after use) sums them in a fixed order.
 #include <cstdio>
+#include <cstdlib>
+#include <cstring>
 #include <type_traits>
 
 #include "common.cuh"
@@ -278,11 +280,11 @@ struct WsLayout {
 
 }  // namespace w8
 
-bool w8a16_stream_eligible(int M, int N, int K, int group);
-size_t w8a16_stream_partial_bytes(int M, int N, int K);
-int w8a16_stream_launch(const void* x, int64_t x_srow, const int8_t* w, const void* s, int s_dtype, const void* bias,
-                        void* y, int64_t y_srow, int M, int N, int K, int act_dtype, int* counters, float* part,
-                        int* err, cudaStream_t st);
+bool w8a16_umma_eligible(int M, int N, int K, int group);
+size_t w8a16_umma_partial_bytes(int M, int N, int K);
+int w8a16_umma_launch(const void* x, int64_t x_srow, const int8_t* w, const void* s, int s_dtype, const void* bias,
+                      void* y, int64_t y_srow, int M, int N, int K, int act_dtype, float* part, int* err,
+                      cudaStream_t st);
 
 namespace w8 {
 
@@ -291,8 +293,7 @@ namespace w8 {
 // every call leaves them at 0).
 constexpr int kCounterCap = 65536;  // output tiles
 
-// Both paths share the counter region at offset 0; the streaming path keeps an error
-// word right after it and its partials after that.
+// Split-K partials of the register kernel follow the counter region.
 static WsLayout ws_layout(int M, int N, int K) {
     Plan pl = plan(M, N, K);
     WsLayout w;
@@ -304,11 +305,20 @@ static WsLayout ws_layout(int M, int N, int K) {
     return w;
 }
 
-constexpr size_t kStreamErrOffset = 256 * 1024;            // == align_up(4 * kCounterCap, 256)
-constexpr size_t kStreamPartOffset = kStreamErrOffset + 256;
+// The tcgen05 path keeps an error word after the counter region and its partials after that.
+constexpr size_t kUmmaErrOffset = 256 * 1024;  // == align_up(4 * kCounterCap, 256)
+constexpr size_t kUmmaPartOffset = kUmmaErrOffset + 256;
 
-static size_t stream_ws_bytes(int M, int N, int K) {
-    return align_up(kStreamPartOffset + w8a16_stream_partial_bytes(M, N, K), 256);
+static size_t umma_ws_bytes(int M, int N, int K) {
+    return align_up(kUmmaPartOffset + w8a16_umma_partial_bytes(M, N, K), 256);
+}
+
+// Kernel choice: the tcgen05 kernel (per-channel scales, M > 16, K % 128 == 0) unless
+// SDB_W8A16_KERNEL=mma forces the register kernel (read per call: tests switch it).
+static bool use_umma(int M, int N, int K, int group) {
+    const char* e = getenv("SDB_W8A16_KERNEL");
+    if (e && !strcmp(e, "mma")) return false;
+    return w8a16_umma_eligible(M, N, K, group);
 }
 
 template <typename T>
@@ -337,8 +347,8 @@ using namespace sdb;
 extern "C" size_t sdb_w8a16_workspace_size(int M, int N, int K) {
     if (M <= 0 || N <= 0 || K <= 0 || K % w8::KC) return 256;
     size_t total = w8::ws_layout(M, N, K).total;
-    if (w8a16_stream_eligible(M, N, K, 0)) {
-        const size_t s = w8::stream_ws_bytes(M, N, K);
+    if (w8a16_umma_eligible(M, N, K, 0)) {
+        const size_t s = w8::umma_ws_bytes(M, N, K);
         if (s > total) total = s;
     }
     return total;
@@ -373,16 +383,16 @@ extern "C" int sdb_w8a16_linear(const void* x, int64_t x_srow, const int8_t* qwe
         return SDB_ERR_INVALID_ARG;
     }
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    if (w8a16_stream_eligible(M, N, K, group_size)) {
-        const size_t need = w8::stream_ws_bytes(M, N, K);
+    if (w8::use_umma(M, N, K, group_size)) {
+        const size_t need = w8::umma_ws_bytes(M, N, K);
         if (workspace_bytes < need) {
             set_last_error("workspace too small: need %zu bytes, got %zu", need, workspace_bytes);
             return SDB_ERR_WORKSPACE;
         }
         uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
-        return w8a16_stream_launch(x, x_srow, qweight, scale, scale_dtype, bias, y, y_srow, M, N, K, act_dtype,
-                                   reinterpret_cast<int*>(ws), reinterpret_cast<float*>(ws + w8::kStreamPartOffset),
-                                   reinterpret_cast<int*>(ws + w8::kStreamErrOffset), st);
+        return w8a16_umma_launch(x, x_srow, qweight, scale, scale_dtype, bias, y, y_srow, M, N, K, act_dtype,
+                                 reinterpret_cast<float*>(ws + w8::kUmmaPartOffset),
+                                 reinterpret_cast<int*>(ws + w8::kUmmaErrOffset), st);
     }
     w8::WsLayout wl = w8::ws_layout(M, N, K);
     if (workspace_bytes < wl.total) {

@@ -17,6 +17,17 @@ pytestmark = pytest.mark.gpu
 TOL = dict(rtol=2e-2, atol=2e-3)
 
 
+@pytest.fixture(autouse=True, params=["auto", "mma"])
+def kernel_choice(request, monkeypatch):
+    """Every test runs on the default kernel (tcgen05 for M > 16 where the shape allows)
+    and on the register kernel (SDB_W8A16_KERNEL=mma)."""
+    if request.param == "auto":
+        monkeypatch.delenv("SDB_W8A16_KERNEL", raising=False)
+    else:
+        monkeypatch.setenv("SDB_W8A16_KERNEL", request.param)
+    return request.param
+
+
 def _ref(x, q, s, bias=None, granularity="per_channel", group_size=128):
     w = (q.double() * s.double().unsqueeze(1) if granularity == "per_channel" else
          (q.double().view(q.shape[0], -1, group_size) * s.double().unsqueeze(-1)).view(q.shape))
