@@ -186,7 +186,6 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const uint32_t fb = bar.rfull0 + 8 * r.slot;
                 mbar_arrive_expect_tx(fb, (uint32_t)p.raw_bytes);
                 tma_load_2d(st, &wmap, fb, kt * KT, ft * FROWS, wpol);
-                tma_load_2d(st + WBOX, &wmap, fb, kt * KT + 64, ft * FROWS, wpol);
                 tma_load_2d(st + 2 * WBOX, &xmap, fb, kt * KT, 0, xpol);
                 tma_load_2d(st + 2 * WBOX + p.xbox, &xmap, fb, kt * KT + 64, 0, xpol);
                 r.next(NR);
@@ -259,7 +258,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int q = warp & 3;           // TMEM lane quarter of this warp
         const uint32_t lane_addr = (uint32_t)(32 * q) << 16;
         const int row_epi = 32 * q + lane;  // feature row whose accumulator this thread reads
-        const int rs = (cr >> 1) & 3, sw = cr & 7;
+        const int sw = cr & 7;
         bool ok = true;
         Ring r, a;
         int ga = 0;  // converted tiles so far
@@ -271,13 +270,13 @@ __global__ void __launch_bounds__(THREADS, 1)
             for (int kt = kt0; kt < kt1; ++kt, ++ga) {
                 if (ok && !mbar_wait(bar.rfull0 + 8 * r.slot, r.phase)) ok = false;
                 if (ok && ga >= NA && !mbar_wait(bar.aempty0 + 8 * a.slot, a.phase ^ 1u)) ok = false;
-                // raw row cr of box kh: 64 B, 16-byte chunk j at j ^ ((cr >> 1) & 3) (64-byte
-                // swizzle); converted row cr of half kh: 128 B, chunk c at c ^ (cr & 7)
-                const uint8_t* wr = rraw + r.slot * p.raw_bytes + kh * WBOX + cr * 64;
+                // raw row cr: 128 B, 16-byte chunk j (k 16j .. 16j+15) at j ^ (cr & 7);
+                // converted row cr of half kh: 128 B, chunk c at c ^ (cr & 7) (both 128-byte swizzle)
+                const uint8_t* wr = rraw + r.slot * p.raw_bytes + cr * 128;
                 uint8_t* ar = araw + a.slot * ATILE + kh * AHALF + cr * 128;
                 uint4 v[4];
 #pragma unroll
-                for (int j = 0; j < 4; ++j) v[j] = *reinterpret_cast<const uint4*>(wr + ((j ^ rs) << 4));
+                for (int j = 0; j < 4; ++j) v[j] = *reinterpret_cast<const uint4*>(wr + (((4 * kh + j) ^ sw) << 4));
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {  // k 16j .. 16j+15 of this half
                     uint32_t o[8];
@@ -417,9 +416,9 @@ int w8a16_umma_launch(const void* x, int64_t x_srow, const int8_t* w, const void
     {
         cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)N};
         cuuint64_t strides[1] = {(cuuint64_t)K};
-        cuuint32_t box[2] = {64, (cuuint32_t)w8u::FROWS};  // one 64-k box (64 B <= the swizzle span)
+        cuuint32_t box[2] = {(cuuint32_t)w8u::KT, (cuuint32_t)w8u::FROWS};  // 128 k x 128 rows, full 128-B rows
         int rc = encode_tensor_map(&wm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<int8_t*>(w), dims, strides, box,
-                                   CU_TENSOR_MAP_SWIZZLE_64B);
+                                   CU_TENSOR_MAP_SWIZZLE_128B);
         if (rc) return rc;
     }
     const CUtensorMapDataType dt = act_dtype == SDB_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
