@@ -32,6 +32,7 @@ extern "C" {
 #define SDB_KERR_BLOCK_ID      0x2 /* block table entry outside [0, num_blocks)    */
 #define SDB_KERR_TIMEOUT       0x4 /* a bounded wait gave up                       */
 #define SDB_KERR_TOKEN         0x8 /* draft token outside [0, vocab)               */
+#define SDB_KERR_SLOT          0x10 /* fused store: slot differs from the position's */
 
 /* ---- dtypes --------------------------------------------------------------- */
 #define SDB_F32   0
@@ -154,6 +155,39 @@ int sdb_store_kvcache(const void* key, int64_t key_stride_tok, int64_t key_strid
                       int64_t kv_stride_block, int64_t kv_stride_page, int64_t kv_stride_head,
                       const int32_t* slot_mapping, int N, int Hkv, int D, int page, int num_blocks,
                       int dtype, void* workspace, void* stream);
+
+/* Fused store + attention: the step's new K / V rows go into the paged cache and
+ * the queries attend over it, in one call.  The result equals sdb_store_kvcache
+ * (key, value, ..., slot_mapping, N = B * n_q) followed by sdb_paged_attention
+ * with the remaining arguments.
+ * Replaces the store_kvcache + attention pair of Attention.forward
+ *                                           nanovllm/layers/attention.py:59-81.
+ *   key, value   (B*n_q, Hkv, D): row b*n_q + i is new token i of sequence b, at
+ *                cache position cache_seqlens[b] - n_q + i (strides in elements)
+ *   slot_mapping (B*n_q) int32: -1 (skip the row) or the slot the block table
+ *                gives that position (nanovllm/engine/model_runner.py:469-476
+ *                for decode, :537-548 for verify)
+ * On the tcgen05 path the attention kernel writes the rows itself: the CTA whose
+ * key range holds a row's position writes it just before the TMA load of that
+ * tile, so the row costs no extra launch and no second read.  A slot that is
+ * neither -1 nor the position's own slot is still written and sets SDB_KERR_SLOT
+ * (the attention then reads the position's own slot, as a separate store
+ * followed by attention would).  The other paths launch the store kernel and
+ * then attention.  No other sequence's block table may name a block that
+ * receives a new row in the same call (the reference's tail blocks are private). */
+int sdb_paged_attention_store(const void* q, int64_t q_stride_row, int64_t q_stride_head,
+                              const void* key, int64_t key_stride_tok, int64_t key_stride_head,
+                              const void* value, int64_t value_stride_tok, int64_t value_stride_head,
+                              const int32_t* slot_mapping,
+                              void* k_cache, void* v_cache,
+                              int64_t kv_stride_block, int64_t kv_stride_page, int64_t kv_stride_head,
+                              const int32_t* block_tables, int64_t bt_stride,
+                              const int32_t* cache_seqlens,
+                              void* out, int64_t o_stride_row, int64_t o_stride_head,
+                              int B, int n_q, int Hq, int Hkv, int D, int page,
+                              int max_blocks, int num_blocks,
+                              float softmax_scale, int dtype, int splits,
+                              void* workspace, size_t workspace_bytes, void* stream);
 
 /* =========================================================================
  * verify_batch: lossless rejection sampling of k drafted tokens.

@@ -56,6 +56,11 @@ SIGNATURES = {
         _c_p, _c_i64, _c_i64, _c_p, _c_p, _c_i64, _c_i64, _c_i64, _c_p, _c_i64, _c_p,
         _c_p, _c_i64, _c_i64, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32,
         _c_f32, _c_i32, _c_i32, _c_p, _c_sz, _c_p]),
+    "sdb_paged_attention_store": (_c_i32, [
+        _c_p, _c_i64, _c_i64, _c_p, _c_i64, _c_i64, _c_p, _c_i64, _c_i64, _c_p,
+        _c_p, _c_p, _c_i64, _c_i64, _c_i64, _c_p, _c_i64, _c_p,
+        _c_p, _c_i64, _c_i64, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32,
+        _c_f32, _c_i32, _c_i32, _c_p, _c_sz, _c_p]),
     "sdb_paged_attention_noalloc": (_c_i32, [
         _c_p, _c_i64, _c_i64, _c_p, _c_p, _c_i64, _c_i64, _c_i64, _c_p, _c_i64, _c_p,
         _c_p, _c_i64, _c_i64, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32,

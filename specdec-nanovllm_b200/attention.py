@@ -52,12 +52,19 @@ def default_splits(B, n_q, Hq, Hkv, D, page, max_blocks, dtype: torch.dtype) -> 
 def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                     block_tables: torch.Tensor, cache_seqlens: torch.Tensor, softmax_scale: float,
                     n_q: int = 1, splits: int = 0, out: torch.Tensor | None = None,
-                    workspace: torch.Tensor | None = None, layout: str = "interleaved") -> torch.Tensor:
+                    workspace: torch.Tensor | None = None, layout: str = "interleaved",
+                    k_new: torch.Tensor | None = None, v_new: torch.Tensor | None = None,
+                    slot_mapping: torch.Tensor | None = None) -> torch.Tensor:
     """Decode (n_q = 1) or verify (n_q = k+1) attention over a paged KV cache.
 
     q (B*n_q, Hq, D); k_cache / v_cache (num_blocks, page, Hkv, D); block_tables
     (B, max_blocks) int32 (-1 padded); cache_seqlens (B,) int32, the cache length
     including the n_q new tokens.  Row r of sequence b sees keys j <= L_b - n_q + r.
+
+    With ``k_new`` / ``v_new`` (B*n_q, Hkv, D) and ``slot_mapping`` (B*n_q,) the
+    call first stores the new rows like ``store_kvcache`` -- row b*n_q + i is the
+    token at position L_b - n_q + i, its slot -1 or that position's slot -- fused
+    into the attention kernel where the tcgen05 path runs (one launch).
     """
     _lib.require_cuda(q, k_cache, v_cache, block_tables, cache_seqlens)
     if q.dim() != 3:
@@ -90,13 +97,37 @@ def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tenso
     need = int(L.sdb_paged_attention_workspace_size(B, n_q, Hq, Hkv, D, splits))
     if workspace is None:
         workspace = _lib.WORKSPACES.get(q.device, "attention", need)
-    rc = L.sdb_paged_attention(
-        q.data_ptr(), q.stride(0), q.stride(1), k_cache.data_ptr(), v_cache.data_ptr(), sb, sp, sh,
+    if k_new is None and v_new is None and slot_mapping is None:
+        rc = L.sdb_paged_attention(
+            q.data_ptr(), q.stride(0), q.stride(1), k_cache.data_ptr(), v_cache.data_ptr(), sb, sp,
+            sh, block_tables.data_ptr(), block_tables.stride(0), cache_seqlens.data_ptr(),
+            out.data_ptr(), out.stride(0), out.stride(1), B, n_q, Hq, Hkv, D, page, max_blocks, nb,
+            float(softmax_scale), dt, splits, workspace.data_ptr(), workspace.numel(),
+            _lib.stream_of(q))
+        _lib.check(rc, "sdb_paged_attention")
+        return out
+    if k_new is None or v_new is None or slot_mapping is None:
+        raise ValueError("k_new, v_new and slot_mapping go together")
+    _lib.require_cuda(k_new, v_new, slot_mapping)
+    if k_new.shape != (B * n_q, Hkv, D) or v_new.shape != k_new.shape:
+        raise ValueError(f"k_new / v_new must be ({B * n_q}, {Hkv}, {D}), got "
+                         f"{tuple(k_new.shape)} / {tuple(v_new.shape)}")
+    if k_new.dtype != q.dtype or v_new.dtype != q.dtype:
+        raise ValueError("k_new / v_new dtype differs from q")
+    if k_new.stride(-1) != 1 or v_new.stride(-1) != 1:
+        raise ValueError("k_new / v_new rows must be contiguous")
+    if slot_mapping.numel() != B * n_q:
+        raise ValueError(f"slot_mapping must have {B * n_q} entries, got {slot_mapping.numel()}")
+    slots = slot_mapping.to(torch.int32).contiguous()
+    rc = L.sdb_paged_attention_store(
+        q.data_ptr(), q.stride(0), q.stride(1), k_new.data_ptr(), k_new.stride(0), k_new.stride(1),
+        v_new.data_ptr(), v_new.stride(0), v_new.stride(1), slots.data_ptr(),
+        k_cache.data_ptr(), v_cache.data_ptr(), sb, sp, sh,
         block_tables.data_ptr(), block_tables.stride(0), cache_seqlens.data_ptr(),
         out.data_ptr(), out.stride(0), out.stride(1), B, n_q, Hq, Hkv, D, page, max_blocks, nb,
         float(softmax_scale), dt, splits, workspace.data_ptr(), workspace.numel(),
         _lib.stream_of(q))
-    _lib.check(rc, "sdb_paged_attention")
+    _lib.check(rc, "sdb_paged_attention_store")
     return out
 
 
@@ -245,7 +276,27 @@ class Attention(nn.Module):
     def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor):
         context = get_context()
         k_cache, v_cache = self.k_cache, self.v_cache
-        if k_cache.numel() and v_cache.numel():
+        has_cache = bool(k_cache.numel() and v_cache.numel())
+        if has_cache and context.block_tables is not None and context.slot_mapping is not None:
+            # decode / verify: the store of this step's rows runs inside the attention launch
+            if context.is_prefill:
+                B = context.cu_seqlens_q.numel() - 1
+                n_q = int(context.max_seqlen_q)
+                if q.shape[0] == B * n_q:
+                    seqlens = (context.cu_seqlens_k[1:] - context.cu_seqlens_k[:-1]).to(torch.int32)
+                    return paged_attention(q, k_cache, v_cache, context.block_tables, seqlens,
+                                           self.scale, n_q=n_q, k_new=k, v_new=v,
+                                           slot_mapping=context.slot_mapping)
+            else:
+                q3 = q.unsqueeze(0) if q.dim() == 2 else q
+                k3 = k.unsqueeze(0) if k.dim() == 2 else k
+                v3 = v.unsqueeze(0) if v.dim() == 2 else v
+                out = paged_attention(q3, k_cache, v_cache, context.block_tables,
+                                      context.context_lens.to(torch.int32), self.scale, n_q=1,
+                                      k_new=k3, v_new=v3, slot_mapping=context.slot_mapping)
+                # the reference's shape: (B, 1, Hq, D), also for a single (Hq, D) query
+                return out.view(q3.shape[0], 1, *q3.shape[1:])
+        if has_cache:
             store_kvcache(k, v, k_cache, v_cache, context.slot_mapping)
         if context.is_prefill:
             if context.block_tables is None:

@@ -779,17 +779,67 @@ int make_maps(CUtensorMap* km, CUtensorMap* vm, const void* k_cache, const void*
     return encode_tensor_map(vm, dt, 4, const_cast<void*>(v_cache), dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-}  // namespace
+// The new rows of a fused store + attention call (strides in elements).
+struct StoreArgs {
+    const void* key;
+    int64_t ks_tok, ks_head;
+    const void* value;
+    int64_t vs_tok, vs_head;
+    const int32_t* slots;
+};
 
-extern "C" int sdb_paged_attention(const void* q, int64_t q_srow, int64_t q_shead, const void* k_cache,
-                                   const void* v_cache, int64_t sb, int64_t sp, int64_t sh,
-                                   const int32_t* block_tables, int64_t bt_stride, const int32_t* cache_seqlens,
-                                   void* out, int64_t o_srow, int64_t o_shead, int B, int n_q, int Hq, int Hkv,
-                                   int D_, int page, int max_blocks, int num_blocks, float softmax_scale,
-                                   int dtype, int splits, void* workspace, size_t workspace_bytes, void* stream) {
+int check_store(const void* key, int64_t ks_tok, int64_t ks_head, const void* value, int64_t vs_tok,
+                int64_t vs_head, const void* k_cache, const void* v_cache, int64_t sb, int64_t sp, int64_t sh,
+                const int32_t* slots, int N, int Hkv, int D_, int page, int num_blocks, int dtype,
+                const void* workspace) {
+    if (!key || !value || !k_cache || !v_cache || !slots || !workspace || N < 0 || Hkv <= 0 || D_ <= 0 ||
+        page <= 0 || num_blocks <= 0) {
+        set_last_error("bad arguments to store_kvcache");
+        return SDB_ERR_INVALID_ARG;
+    }
+    if (dtype != SDB_F32 && dtype != SDB_BF16 && dtype != SDB_F16) {
+        set_last_error("dtype %d not supported", dtype);
+        return SDB_ERR_UNSUPPORTED;
+    }
+    const int elem = dtype == SDB_F32 ? 4 : 2;
+    auto mis = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) != 0; };
+    if (((D_ * elem) & 15) || mis(key) || mis(value) || mis(k_cache) || mis(v_cache) || ((ks_tok * elem) & 15) ||
+        ((ks_head * elem) & 15) || ((vs_tok * elem) & 15) || ((vs_head * elem) & 15) || ((sb * elem) & 15) ||
+        ((sp * elem) & 15) || ((sh * elem) & 15)) {
+        set_last_error("store_kvcache needs 16-byte aligned rows and strides");
+        return SDB_ERR_INVALID_ARG;
+    }
+    return SDB_OK;
+}
+
+int launch_store(const StoreArgs& a, void* k_cache, void* v_cache, int64_t sb, int64_t sp, int64_t sh, int N,
+                 int Hkv, int D_, int page, int num_blocks, int dtype, void* workspace, cudaStream_t st) {
+    if (N == 0) return SDB_OK;
+    const int elem = dtype == SDB_F32 ? 4 : 2;
+    const int row_bytes = D_ * elem;
+    int threads = Hkv * (row_bytes / 16);
+    threads = threads > 256 ? 256 : (threads < 32 ? 32 : threads);
+    store_kvcache_kernel<<<N, threads, 0, st>>>(
+        reinterpret_cast<const uint8_t*>(a.key), a.ks_tok, a.ks_head, reinterpret_cast<const uint8_t*>(a.value),
+        a.vs_tok, a.vs_head, reinterpret_cast<uint8_t*>(k_cache), reinterpret_cast<uint8_t*>(v_cache), sb, sp, sh,
+        a.slots, Hkv, row_bytes, page, num_blocks, elem, reinterpret_cast<int*>(workspace));
+    return cuda_status(cudaGetLastError(), "store_kvcache launch");
+}
+
+int attention_impl(const void* q, int64_t q_srow, int64_t q_shead, const void* k_cache, const void* v_cache,
+                   int64_t sb, int64_t sp, int64_t sh, const int32_t* block_tables, int64_t bt_stride,
+                   const int32_t* cache_seqlens, void* out, int64_t o_srow, int64_t o_shead, int B, int n_q, int Hq,
+                   int Hkv, int D_, int page, int max_blocks, int num_blocks, float softmax_scale, int dtype,
+                   int splits, void* workspace, size_t workspace_bytes, void* stream, const StoreArgs* store) {
     int rc = validate(q, k_cache, v_cache, block_tables, cache_seqlens, B, n_q, Hq, Hkv, D_, page, max_blocks,
                       num_blocks, q_srow, q_shead, sb, sp, sh, bt_stride, workspace);
     if (rc) return rc;
+    if (store) {
+        rc = check_store(store->key, store->ks_tok, store->ks_head, store->value, store->vs_tok, store->vs_head,
+                         k_cache, v_cache, sb, sp, sh, store->slots, B * n_q, Hkv, D_, page, num_blocks, dtype,
+                         workspace);
+        if (rc) return rc;
+    }
     if (!out || o_shead < D_) {
         set_last_error("bad output pointer or stride");
         return SDB_ERR_INVALID_ARG;
@@ -833,7 +883,26 @@ extern "C" int sdb_paged_attention(const void* q, int64_t q_srow, int64_t q_shea
             set_last_error("q rows and the KV cache must be 16-byte aligned");
             return SDB_ERR_INVALID_ARG;
         }
+        if (store) {  // the attention kernel writes the new rows itself
+            p.slots = store->slots;
+            p.new_k = reinterpret_cast<const uint8_t*>(store->key);
+            p.new_v = reinterpret_cast<const uint8_t*>(store->value);
+            p.nk_stok = store->ks_tok * 2;
+            p.nk_shead = store->ks_head * 2;
+            p.nv_stok = store->vs_tok * 2;
+            p.nv_shead = store->vs_head * 2;
+            p.kc = reinterpret_cast<uint8_t*>(const_cast<void*>(k_cache));
+            p.vc = reinterpret_cast<uint8_t*>(const_cast<void*>(v_cache));
+            p.c_sb = sb * 2;
+            p.c_sp = sp * 2;
+            p.c_sh = sh * 2;
+        }
         return launch_umma(k_cache, v_cache, dtype, sb, sp, sh, p, workspace, workspace_bytes, splits, st);
+    }
+    if (store) {  // other paths: the store kernel, then attention
+        rc = launch_store(*store, const_cast<void*>(k_cache), const_cast<void*>(v_cache), sb, sp, sh, B * n_q, Hkv,
+                          D_, page, num_blocks, dtype, workspace, st);
+        if (rc) return rc;
     }
 
     if (mma_path(dtype, D_, page, R)) {
@@ -906,6 +975,33 @@ extern "C" int sdb_paged_attention(const void* q, int64_t q_srow, int64_t q_shea
     return cuda_status(cudaGetLastError(), "pa_simt_kernel launch");
 }
 
+}  // namespace
+
+extern "C" int sdb_paged_attention(const void* q, int64_t q_srow, int64_t q_shead, const void* k_cache,
+                                   const void* v_cache, int64_t sb, int64_t sp, int64_t sh,
+                                   const int32_t* block_tables, int64_t bt_stride, const int32_t* cache_seqlens,
+                                   void* out, int64_t o_srow, int64_t o_shead, int B, int n_q, int Hq, int Hkv,
+                                   int D_, int page, int max_blocks, int num_blocks, float softmax_scale,
+                                   int dtype, int splits, void* workspace, size_t workspace_bytes, void* stream) {
+    return attention_impl(q, q_srow, q_shead, k_cache, v_cache, sb, sp, sh, block_tables, bt_stride, cache_seqlens,
+                          out, o_srow, o_shead, B, n_q, Hq, Hkv, D_, page, max_blocks, num_blocks, softmax_scale,
+                          dtype, splits, workspace, workspace_bytes, stream, nullptr);
+}
+
+extern "C" int sdb_paged_attention_store(const void* q, int64_t q_srow, int64_t q_shead, const void* key,
+                                         int64_t ks_tok, int64_t ks_head, const void* value, int64_t vs_tok,
+                                         int64_t vs_head, const int32_t* slot_mapping, void* k_cache, void* v_cache,
+                                         int64_t sb, int64_t sp, int64_t sh, const int32_t* block_tables,
+                                         int64_t bt_stride, const int32_t* cache_seqlens, void* out, int64_t o_srow,
+                                         int64_t o_shead, int B, int n_q, int Hq, int Hkv, int D_, int page,
+                                         int max_blocks, int num_blocks, float softmax_scale, int dtype, int splits,
+                                         void* workspace, size_t workspace_bytes, void* stream) {
+    const StoreArgs a{key, ks_tok, ks_head, value, vs_tok, vs_head, slot_mapping};
+    return attention_impl(q, q_srow, q_shead, k_cache, v_cache, sb, sp, sh, block_tables, bt_stride, cache_seqlens,
+                          out, o_srow, o_shead, B, n_q, Hq, Hkv, D_, page, max_blocks, num_blocks, softmax_scale,
+                          dtype, splits, workspace, workspace_bytes, stream, &a);
+}
+
 extern "C" int sdb_paged_attention_readonly(const void* q, int64_t q_srow, int64_t q_shead, const void* k_cache,
                                             const void* v_cache, int64_t sb, int64_t sp, int64_t sh,
                                             const int32_t* block_tables, int64_t bt_stride,
@@ -964,29 +1060,10 @@ extern "C" int sdb_store_kvcache(const void* key, int64_t ks_tok, int64_t ks_hea
                                  const int32_t* slot_mapping, int N, int Hkv, int D_, int page, int num_blocks,
                                  int dtype, void* workspace, void* stream) {
     if (N == 0) return SDB_OK;
-    if (!key || !value || !k_cache || !v_cache || !slot_mapping || !workspace || N < 0 || Hkv <= 0 || D_ <= 0 ||
-        page <= 0 || num_blocks <= 0) {
-        set_last_error("bad arguments to sdb_store_kvcache");
-        return SDB_ERR_INVALID_ARG;
-    }
-    const int elem = dtype == SDB_F32 ? 4 : 2;
-    if (dtype != SDB_F32 && dtype != SDB_BF16 && dtype != SDB_F16) {
-        set_last_error("dtype %d not supported", dtype);
-        return SDB_ERR_UNSUPPORTED;
-    }
-    const int row_bytes = D_ * elem;
-    auto mis = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) != 0; };
-    if ((row_bytes & 15) || mis(key) || mis(value) || mis(k_cache) || mis(v_cache) || ((ks_tok * elem) & 15) ||
-        ((ks_head * elem) & 15) || ((vs_tok * elem) & 15) || ((vs_head * elem) & 15) || ((sb * elem) & 15) ||
-        ((sp * elem) & 15) || ((sh * elem) & 15)) {
-        set_last_error("store_kvcache needs 16-byte aligned rows and strides");
-        return SDB_ERR_INVALID_ARG;
-    }
-    int threads = Hkv * (row_bytes / 16);
-    threads = threads > 256 ? 256 : (threads < 32 ? 32 : threads);
-    store_kvcache_kernel<<<N, threads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-        reinterpret_cast<const uint8_t*>(key), ks_tok, ks_head, reinterpret_cast<const uint8_t*>(value), vs_tok,
-        vs_head, reinterpret_cast<uint8_t*>(k_cache), reinterpret_cast<uint8_t*>(v_cache), sb, sp, sh, slot_mapping,
-        Hkv, row_bytes, page, num_blocks, elem, reinterpret_cast<int*>(workspace));
-    return cuda_status(cudaGetLastError(), "store_kvcache launch");
+    int rc = check_store(key, ks_tok, ks_head, value, vs_tok, vs_head, k_cache, v_cache, sb, sp, sh, slot_mapping, N,
+                         Hkv, D_, page, num_blocks, dtype, workspace);
+    if (rc) return rc;
+    const StoreArgs a{key, ks_tok, ks_head, value, vs_tok, vs_head, slot_mapping};
+    return launch_store(a, k_cache, v_cache, sb, sp, sh, N, Hkv, D_, page, num_blocks, dtype, workspace,
+                        reinterpret_cast<cudaStream_t>(stream));
 }

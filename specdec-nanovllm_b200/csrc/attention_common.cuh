@@ -32,6 +32,16 @@ struct Params {
     // splits instead), all sequences' slots, and the CTA groups (Hkv CTAs each) sharing them
     int flat_T, flat_grid;
     long long flat_total;
+    // tcgen05 path, fused store_kvcache: the step's new K / V rows (token b * n_q + i,
+    // at cache position seqlen(b) - n_q + i) and their slots; slots == nullptr when the
+    // launch stores nothing.  Strides in bytes.
+    const int* slots;
+    const uint8_t* new_k;
+    const uint8_t* new_v;
+    uint8_t* kc;
+    uint8_t* vc;
+    int64_t nk_stok, nk_shead, nv_stok, nv_shead;
+    int64_t c_sb, c_sp, c_sh;
 };
 
 struct WsLayout {

@@ -20,7 +20,9 @@
 // Warp roles (320 threads, one CTA per SM, persistent over work items):
 //   warp 0      TMA producer: Q of each item, K/V tiles of 128 keys into a 3-stage ring
 //   warp 1      TMEM owner and MMA issuer (one thread)
-//   warps 2..9  softmax: thread = one TMEM lane (a key of S^T, a dim of O^T) and
+//   warps 2..9  (fused store_kvcache only) first copy the step's new K/V rows of
+//               the CTA's items into the cache, then
+//               softmax: thread = one TMEM lane (a key of S^T, a dim of O^T) and
 //               16 of the 32 columns (rows); column max / sum by an in-warp
 //               transpose reduction + a 4-warp exchange; lazy rescale (O is
 //               rescaled only when a row max grows by more than 2^8, exact
@@ -30,6 +32,7 @@
 // LSE-merges the partials.  Every wait is bounded and reports SDB_KERR_TIMEOUT
 // instead of hanging.
 #include <cfloat>
+#include <climits>
 
 #include "attention_common.cuh"
 #include "umma.cuh"
@@ -57,8 +60,8 @@ constexpr int OFF_Q = UNS * USTAGE;       // two Q^T buffers: item i uses buffer
 constexpr int OFF_RED = OFF_Q + 2 * QBUF;             // red_max[4][32], red_sum[4][32]
 constexpr int kMaxUmmaSplits = 16;
 constexpr int OFF_BAR = OFF_RED + 2 * 4 * 32 * 4;
-// barriers: full[3] empty[3] s_full[2] s_free[2] p_full q_ready[2] q_free[2] fin
-constexpr int NBAR = UNS * 2 + 2 + 2 + 1 + 2 + 2 + 1;
+// barriers: full[3] empty[3] s_full[2] s_free[2] p_full q_ready[2] q_free[2] fin stored
+constexpr int NBAR = UNS * 2 + 2 + 2 + 1 + 2 + 2 + 1 + 1;
 constexpr int OFF_TMEM = OFF_BAR + NBAR * 8;
 constexpr int SMEM_BYTES = OFF_TMEM + 16 + 1024;  // + alignment slack
 // TMEM columns: S^T buffers [0, 64), O^T heads / residuals [64, 96) / [96, 128)
@@ -69,7 +72,7 @@ constexpr int SOFTMAX_WARPS = SOFTMAX_THREADS / 32;  // one mbarrier arrival per
 constexpr int THREADS = 64 + SOFTMAX_THREADS;
 
 struct Bars {
-    uint32_t full0, empty0, sfull0, sfree0, pfull, qready0, qfree0, fin;
+    uint32_t full0, empty0, sfull0, sfree0, pfull, qready0, qfree0, fin, stored;
 };
 
 SDB_DEV Bars bars_at(uint32_t base) {
@@ -82,6 +85,7 @@ SDB_DEV Bars bars_at(uint32_t base) {
     b.qready0 = b.pfull + 8;
     b.qfree0 = b.qready0 + 16;
     b.fin = b.qfree0 + 16;
+    b.stored = b.fin + 8;
     return b;
 }
 
@@ -89,7 +93,7 @@ SDB_DEV Bars bars_at(uint32_t base) {
 // CTA.  `direct`: the CTA holds every key of the pair and writes the output itself;
 // otherwise it writes partial `slot` of the pair for pa_umma_merge_kernel.
 struct Item {
-    int b, kvh, slot, L, k0, k1, ntiles, span;
+    int b, kvh, slot, L, k0, k1, kend, ntiles, span;  // kend: k1 before clamping to L
     bool direct;
 };
 
@@ -99,6 +103,7 @@ SDB_DEV Item make_item(const Params& p, int pair, int k0, int k1, int slot, bool
     x.b = pair / p.Hkv;
     x.L = load_len(p, x.b);
     x.k0 = k0;
+    x.kend = k1;
     x.k1 = min(k1, x.L);
     x.ntiles = x.k1 > x.k0 ? (x.k1 - x.k0 + UBN - 1) / UBN : 0;
     x.slot = slot;
@@ -150,6 +155,10 @@ struct WorkIter {
         return make_item(p, it / p.splits, split * p.chunk, split * p.chunk + p.chunk, split, p.splits == 1, 0);
     }
     SDB_DEV void next(const Params& p, const Item& x) { f += p.flat_T > 0 ? x.span : gridDim.x; }
+    // next() without the item (the same span)
+    SDB_DEV void skip(const Params& p) {
+        f += p.flat_T > 0 ? min(p.flat_T - f % p.flat_T, f1 - f) : (int)gridDim.x;
+    }
 };
 
 // Position (item, tile) in the sequence of tiles this CTA processes (items without
@@ -172,6 +181,98 @@ struct TileCursor {
         }
     }
 };
+
+// Fused store_kvcache (nanovllm/layers/attention.py:10-40 followed by the attention
+// of :59-81).  New token i of sequence b (row b * n_q + i of key / value) sits at
+// cache position L - n_q + i.  The item whose unclamped key range [k0, kend) holds
+// that position -- or key 0 for a token at a negative position -- owns the token's
+// kv-head row: the key ranges of a (sequence, kv head) pair partition
+// [0, max_blocks * page), so every row has exactly one owner, and only the owner's
+// CTA reads the tile holding the position.  At kernel start the softmax warps of
+// each CTA copy the rows of all its items to their slots (they would otherwise wait
+// for the first S tile), then arrive on the `stored` barrier; the producer waits on
+// it once, before the TMA load of the first tile holding a new row.  The fused form
+// needs the slot of a token at position p >= 0 to be -1 or the slot the block table
+// gives p; any other slot is still written but sets SDB_KERR_SLOT (the attention
+// reads the position's own slot, as a separate store followed by attention would).
+struct NewRows {
+    int i0, i1;  // tokens [i0, i1) of the item's sequence
+    int tile;    // the item's first tile holding one of their positions
+};
+
+SDB_DEV NewRows new_rows(const Params& p, const Item& x) {
+    NewRows r{0, 0, 0};
+    if (p.slots == nullptr) return r;
+    const int lo = x.L - p.n_q;  // position of token 0
+    r.i0 = x.k0 == 0 ? 0 : max(0, x.k0 - lo);
+    r.i1 = min(p.n_q, x.kend - lo);
+    const int first = max(max(lo, 0), x.k0);
+    r.tile = (first - x.k0) / UBN;
+    return r;
+}
+
+// Warp-wide copy of the item's owned rows (n_q <= 32 tokens): lane u reads token u's
+// slot and checks it, then per token lanes 0..15 copy 16 bytes each of the K row and
+// lanes 16..31 of the V row (head_dim 128 at 16 bits = 256 bytes), eight tokens' loads
+// in flight at a time.
+SDB_DEV void copy_new_rows(const Params& p, const Item& x, const NewRows& nr, int lane) {
+    const int lo = x.L - p.n_q;
+    const int n = nr.i1 - nr.i0;
+    const int tok0 = x.b * p.n_q + nr.i0;
+    int slot = -1;
+    bool bad_blk = false, bad_slot = false;
+    if (lane < n) {
+        slot = p.slots[tok0 + lane];
+        const int pos = lo + nr.i0 + lane;
+        const int want = pos >= 0 ? p.bt[(int64_t)x.b * p.bt_stride + pos / p.page] * p.page + pos % p.page : slot;
+        if (slot >= 0) {
+            if (slot / p.page >= p.num_blocks) {
+                bad_blk = true;
+                slot = -1;
+            } else if (want != slot) {
+                bad_slot = true;
+            }
+        }
+    }
+    const unsigned bb = __ballot_sync(0xffffffffu, bad_blk), bs = __ballot_sync(0xffffffffu, bad_slot);
+    if (lane == 0 && bb) atomicOr(p.err, SDB_KERR_BLOCK_ID);
+    if (lane == 0 && bs) atomicOr(p.err, SDB_KERR_SLOT);
+    const bool isv = lane >= 16;
+    const int c = lane & 15;
+    const uint8_t* src0 = (isv ? p.new_v : p.new_k) + (int64_t)x.kvh * (isv ? p.nv_shead : p.nk_shead) + c * 16;
+    const int64_t src_stok = isv ? p.nv_stok : p.nk_stok;
+    uint8_t* dst0 = (isv ? p.vc : p.kc) + (int64_t)x.kvh * p.c_sh + c * 16;
+    for (int u0 = 0; u0 < n; u0 += 8) {
+        uint4 v[8];
+        uint8_t* dst[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int sl = __shfl_sync(0xffffffffu, slot, (u0 + u) & 31);
+            dst[u] = nullptr;
+            if (u0 + u < n && sl >= 0) {
+                v[u] = __ldg(reinterpret_cast<const uint4*>(src0 + (int64_t)(tok0 + u0 + u) * src_stok));
+                dst[u] = dst0 + (int64_t)(sl / p.page) * p.c_sb + (int64_t)(sl % p.page) * p.c_sp;
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+            if (dst[u]) *reinterpret_cast<uint4*>(dst[u]) = v[u];
+    }
+}
+
+// Softmax warp sw (0..7) copies the new rows of items sw, sw + 8, ... of this CTA,
+// then makes them visible to the async proxy (the producer's TMA loads).
+SDB_DEV void store_new_rows(const Params& p, int sw, int lane) {
+    int k = 0;
+    for (WorkIter w(p); w.valid(); w.skip(p), ++k) {
+        if (k % SOFTMAX_WARPS != sw) continue;
+        const Item x = w.item(p);
+        const NewRows nr = new_rows(p, x);
+        if (nr.i0 < nr.i1) copy_new_rows(p, x, nr, lane);
+    }
+    fence_proxy_async_global();
+    __syncwarp();
+}
 
 // Wait that becomes a no-op once this thread has seen a timeout: the softmax warps
 // keep executing the same sequence of named barriers after a failure (never
@@ -234,6 +335,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             mbar_init(bar.qfree0 + 8 * i, 1);
         }
         mbar_init(bar.fin, 1);
+        mbar_init(bar.stored, SOFTMAX_WARPS);
         fence_mbarrier_init();
     }
     if (warp == 1) {
@@ -259,12 +361,18 @@ __global__ void __launch_bounds__(THREADS, 1)
             const uint64_t qpol = l2_policy_evict_normal();  // every split of a sequence reads Q
             int gt = 0, nq = 0;
             bool ok = true;
+            bool stored = p.slots == nullptr;  // no fused store: nothing to wait for
+            int need_tile = INT_MAX;
             TileCursor ld(p);
             while (ld.valid()) {
                 const int j = ld.x.k0 + ld.t * UBN;
                 // the block id is read before the waits, off the stage-hold path
                 int blk = p.bt[(int64_t)ld.x.b * p.bt_stride + j / p.page];
                 if (ld.t == 0) {
+                    if (!stored) {
+                        const NewRows nr = new_rows(p, ld.x);
+                        need_tile = nr.i0 < nr.i1 ? nr.tile : INT_MAX;
+                    }
                     // Q^T rows (r, g) -> row r*G + g of Q buffer nq & 1, K-major 128-byte swizzle;
                     // the buffer is free once the S MMAs of the item two before have completed
                     const int qb = nq & 1;
@@ -282,6 +390,14 @@ __global__ void __launch_bounds__(THREADS, 1)
                 if (gt >= UNS && !mbar_wait(bar.empty0 + 8 * s, ((gt / UNS) - 1) & 1)) {
                     ok = false;
                     break;
+                }
+                // the fused store's rows are in place before a tile holding one is loaded
+                if (!stored && ld.t >= need_tile) {
+                    if (!mbar_wait(bar.stored, 0)) {
+                        ok = false;
+                        break;
+                    }
+                    stored = true;
                 }
                 if (blk < 0 || blk >= p.num_blocks) {
                     atomicOr(p.err, SDB_KERR_BLOCK_ID);
@@ -390,6 +506,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         // (first tile of an item, or a row max that grew) all warps take the exact path:
         // column max over the 128 keys, new reference = max, partial sums and O rescaled.
         const int sw = warp - 2;            // 0..7
+        if (p.slots != nullptr) {  // fused store_kvcache, before the first S tile arrives
+            store_new_rows(p, sw, lane);
+            if (lane == 0) mbar_arrive(bar.stored);
+        }
         const int qt = warp & 3;
         const int ch = sw >> 2;
         const int c0 = 16 * ch;             // first column (row) of this thread

@@ -21,6 +21,9 @@ SDB_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;"
 // Make this thread's generic-proxy shared-memory writes visible to the async proxy
 // (tensor-core operand reads).
 SDB_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// Make this thread's generic-proxy global-memory writes visible to later async-proxy
+// (TMA) reads of the same addresses.
+SDB_DEV void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
 
 // Warp-wide: allocate `ncols` TMEM columns (power of two >= 32); the base address is written to smem.
 SDB_DEV void tmem_alloc(uint32_t smem_dst, uint32_t ncols) {

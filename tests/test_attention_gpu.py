@@ -339,3 +339,97 @@ def test_attention_module_decode_and_reference_mirrors(pkg, W):
     _check(o_cuda_api, want, BF16_TOL)
     assert o1.shape == (1, 1, 16, 128)
     _check(o1.view(1, 16, 128), want[:1], BF16_TOL)
+
+
+# ------------------------------------------------------------------ fused store + attention
+def _own_slots(case, n_q, page=256):
+    """slot_mapping as prepare_decode / prepare_verify build it (model_runner.py:469-476,
+    :537-548): token i of sequence b -> the slot of position L_b - n_q + i."""
+    bt = case.block_tables.cpu()
+    slots = []
+    for b, L in enumerate(case.cache_seqlens.cpu().tolist()):
+        for pos in range(L - n_q, L):
+            slots.append(int(bt[b, pos // page]) * page + pos % page if pos >= 0 else -1)
+    return slots
+
+
+def _fused_vs_separate(pkg, case, slots, splits=0, seed=5):
+    """The fused call must leave the same cache bits and return the same output bits as
+    store_kvcache followed by paged_attention with the same split count."""
+    n_q, (total, Hq, D) = case.n_q, case.q.shape
+    Hkv = case.k_cache.shape[2]
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    k_new = torch.randn(total, Hkv, D, generator=g).to(case.q.dtype).cuda()
+    v_new = torch.randn(total, Hkv, D, generator=g).to(case.q.dtype).cuda()
+    sm = torch.tensor(slots, dtype=torch.int32, device="cuda")
+    kc1, vc1 = case.k_cache.clone(), case.v_cache.clone()
+    kc2, vc2 = case.k_cache.clone(), case.v_cache.clone()
+    pkg.store_kvcache(k_new, v_new, kc1, vc1, sm)
+    want = pkg.paged_attention(case.q, kc1, vc1, case.block_tables, case.cache_seqlens, case.scale,
+                               n_q=n_q, splits=splits)
+    got = pkg.paged_attention(case.q, kc2, vc2, case.block_tables, case.cache_seqlens, case.scale,
+                              n_q=n_q, splits=splits, k_new=k_new, v_new=v_new, slot_mapping=sm)
+    torch.cuda.synchronize()
+    bits = torch.int32 if case.q.dtype == torch.float32 else torch.int16
+    assert torch.equal(kc1.view(bits), kc2.view(bits)), "K cache differs"
+    assert torch.equal(vc1.view(bits), vc2.view(bits)), "V cache differs"
+    assert torch.equal(want.view(bits), got.view(bits)), "attention output differs"
+    return got, kc2, vc2
+
+
+@pytest.mark.parametrize("splits", [0, 1, 3])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_fused_store_verify(pkg, W, splits, dtype):
+    # new positions inside one tile, across a 128-key tile edge, across a page edge,
+    # fewer keys than new tokens (L < n_q), L == n_q, and a long sequence
+    lens = [300, 131, 260, 3, 7, 1500]
+    case = W.paged_case(lens, 7, seed=41, max_blocks=6, dtype=dtype, **W.QWEN3_4B)
+    slots = _own_slots(case, 7)
+    slots[2] = -1  # a skipped row keeps the old cache content
+    used = set(case.block_tables.flatten().tolist())
+    spare = [b for b in range(case.k_cache.shape[0]) if b not in used][0]
+    for i in range(4):  # the L = 3 sequence's tokens at negative positions are still stored
+        slots[3 * 7 + i] = spare * 256 + 9 * i
+    _fused_vs_separate(pkg, case, slots, splits=splits)
+    assert pkg.attention.error_word() == 0
+
+
+def test_fused_store_decode(pkg, W):
+    case = W.paged_case([513, 64, 1, 256, 257], 1, seed=43, max_blocks=3, **W.QWEN3_06B)
+    slots = _own_slots(case, 1)
+    slots[3] = -1
+    _fused_vs_separate(pkg, case, slots)
+    assert pkg.attention.error_word() == 0
+
+
+def test_fused_store_empty_sequence_and_fp32(pkg, W):
+    """L = 0: the row has no position (nothing reads it) but is still stored, as
+    store_kvcache would; fp32 runs the store kernel + CUDA-core path."""
+    for dtype in (torch.bfloat16, torch.float32):
+        case = W.paged_case([0, 40, 0], 1, seed=44, max_blocks=2, extra_blocks=2, dtype=dtype,
+                            **W.QWEN3_06B)
+        used = set(case.block_tables.flatten().tolist())
+        spare = [b for b in range(case.k_cache.shape[0]) if b not in used]
+        slots = _own_slots(case, 1)
+        slots[0] = spare[0] * 256 + 5
+        slots[2] = spare[1] * 256 + 255
+        got, _, _ = _fused_vs_separate(pkg, case, slots)
+        assert torch.count_nonzero(got[0].float()) == 0 and torch.count_nonzero(got[2].float()) == 0
+        assert pkg.attention.error_word() == 0
+
+
+def test_fused_store_foreign_slot_flags(pkg, W, kernel_choice):
+    """A slot that is not the position's own is written (store semantics) and, on the
+    tcgen05 path, reported with SDB_KERR_SLOT; the attention reads the position's own
+    slot, exactly as a separate store followed by attention does."""
+    case = W.paged_case([200, 90], 4, seed=45, max_blocks=1, extra_blocks=1, **W.QWEN3_4B)
+    used = set(case.block_tables.flatten().tolist())
+    spare = [b for b in range(case.k_cache.shape[0]) if b not in used][0]
+    slots = _own_slots(case, 4)
+    slots[1] = spare * 256 + 17
+    try:
+        _fused_vs_separate(pkg, case, slots)
+        err = pkg.attention.error_word()
+        assert err == (0x10 if kernel_choice == "auto" else 0)
+    finally:
+        pkg.attention.clear_error_word()
