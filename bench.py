@@ -483,6 +483,35 @@ def run_side(args):
                              "unit": "GB/s", "frac": round(gbs / peak, 4),
                              "tflops": round(flops / (ms * 1e-3) / 1e12, 2)},
                 "gpu_launches": 4 * steps}
+    elif args.mode == "sample":
+        # one draft-proposer sampling step (draft_proposer.py:505-510): B rows of bf16 LM-head
+        # logits -> fp32 copy into out_logits[:, s] + Gumbel-max token into cands[:, s]
+        B, V, k = 64, workloads.VOCAB, 6
+        NSET = 8  # 8 x 19.4 MB of logits rotated per step (155 MB > 126 MB L2)
+        gd = torch.Generator(device="cuda").manual_seed(0)
+        lg = [(torch.randn(B, V, generator=gd, device="cuda") * 3.0).to(torch.bfloat16) for _ in range(NSET)]
+        temps = torch.ones(B, 1, device="cuda")
+        out_logits = torch.empty(B, k, V, device="cuda")
+        cands = torch.empty(B, k, dtype=torch.int64, device="cuda")
+        ctr = [0]
+
+        def step():
+            i = ctr[0]
+            ctr[0] += 1
+            pkg.draft_sample_step(lg[i % NSET], temps, out_logits, cands, i % k, seed=1, offset=i)
+        ms = _time_events(step, steps, args.warmup, per_graph=2 * NSET)
+        nbytes = B * V * (2 + 4)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        line = {"metric": "draft sample step HBM GB/s", "value": round(gbs, 2), "unit": "GB/s", "n_gpus": 1,
+                "steps": steps, "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True,
+                "dtype": "bf16 in, f32 copy", "data": "synthetic",
+                "config": {"workload": f"draft_sample_step B={B} V={V} (logits N(0,9) bf16, T=1, in-kernel Philox "
+                                       "noise)", "bytes_per_step": nbytes,
+                           "l2": f"{NSET} logit tensors rotated per step (155 MB > 126 MB L2)"},
+                "roofline": {"bound": "hbm", "achieved": round(gbs, 2), "peak": peak, "peak_kind": peak_kind,
+                             "unit": "GB/s", "frac": round(gbs / peak, 4),
+                             "note": "issue-bound: the Philox noise of every column is most of the instructions"},
+                "gpu_launches": 2 * steps}
     else:  # decode attention
         from oracle.attention import algorithmic_bytes
         B, L = B_PER_GPU, CTX
@@ -512,7 +541,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--skip-cpu", action="store_true", help="omit the CPU baseline leg")
-    ap.add_argument("--mode", choices=["verify_attn", "decode_attn", "verify_batch", "w8a16"],
+    ap.add_argument("--mode", choices=["verify_attn", "decode_attn", "verify_batch", "w8a16", "sample"],
                     default="verify_attn", help="verify_attn is the headline; the others measure the "
                     "secondary kernels of the path on one GPU")
     ap.add_argument("--m", type=int, default=1, help="tokens (M) for --mode w8a16")

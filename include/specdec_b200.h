@@ -217,10 +217,40 @@ int sdb_verify_batch(const float* draft_logits, const float* target_logits,
                      int B, int k, int target_rows, int V,
                      void* workspace, size_t workspace_bytes, void* stream);
 
-/* Philox streams of the sampler written out (test and debugging aid): stream 0
- * as uniforms [rows, cols] or stream 1 as exponentials [rows, cols]. */
+/* Philox streams of the samplers written out (test and debugging aid): stream 0
+ * as uniforms [rows, cols], stream 1 (verify_batch) or 2 (sample) as
+ * exponentials [rows, cols]. */
 int sdb_philox_fill(float* out, int rows, int cols, uint64_t seed, uint64_t offset,
                     int stream_id, void* stream);
+
+/* =========================================================================
+ * sample: Gumbel-max token sampling with exponential noise.
+ *
+ * Replaces Sampler.forward(logits, temperatures)   nanovllm/layers/sampler.py:8-12
+ * and the draft step's sampling + logits copy   nanovllm/spec_decode/draft_proposer.py:505-510
+ *   tokens[b] = argmax_i softmax(logits[b] / T[b])_i / max(E[b, i], 1e-10),  E ~ Exp(1),
+ *   first index on ties (torch.argmax).
+ *
+ *   logits       (B, V) f32 / bf16 / f16 (dtype), rows logits_stride_row elements
+ *                apart, contiguous within a row; converted to float32 exactly
+ *   temperatures (B) float32 or NULL (no division); T > 0 as in the reference
+ *   exponentials (B, V) float32 or NULL: the noise; NULL -> Philox stream 2 keyed
+ *                by (seed, offset), E = -log(U) (sdb_philox_fill, stream_id 2)
+ *   tokens       int64, row b's token at tokens[b * tokens_stride]
+ *   logits_f32   NULL, or (B, V) float32 rows logits_f32_stride_row apart that
+ *                receive logits converted to float32 (the draft step's copy)
+ * workspace: sdb_sample_workspace_size(B, V) bytes, 256-byte aligned (no zeroing
+ * needed).  Two launches (the second a programmatic dependent launch); one read of
+ * the logits.  The inputs are not modified (the reference divides fp32 logits in
+ * place).
+ * ========================================================================= */
+size_t sdb_sample_workspace_size(int B, int V);
+int sdb_sample(const void* logits, int64_t logits_stride_row, int dtype,
+               const float* temperatures, const float* exponentials,
+               uint64_t seed, uint64_t offset,
+               int64_t* tokens, int64_t tokens_stride,
+               float* logits_f32, int64_t logits_f32_stride_row,
+               int B, int V, void* workspace, size_t workspace_bytes, void* stream);
 
 /* =========================================================================
  * W8A16 linear: y = x @ (q * scale)^T (+ bias), int8 weights dequantised in

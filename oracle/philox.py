@@ -1,7 +1,8 @@
 """Counter-based random numbers shared bit-for-bit by the oracle and the GPU sampler.
 
-Test infrastructure only.  The GPU sampler (``csrc/verify_sample.cu``) carries
-its own CUDA restatement of exactly these operations; this module is the checker.
+Test infrastructure only.  The GPU samplers (``csrc/philox.cuh``, used by
+``csrc/verify_sample.cu`` and ``csrc/sampler.cu``) carry their own CUDA
+restatement of exactly these operations; this module is the checker.
 
 Philox4x32-10 is the published generator of Salmon, Moraes, Dror and Shaw,
 "Parallel random numbers: as easy as 1, 2, 3" (SC'11): 10 rounds of
@@ -17,6 +18,8 @@ reference parity tests inject both draws instead):
     value   = word (col % 4) of philox(counter, key)
     stream 0: acceptance uniforms u[b, j]     -> u = (w >> 8) * 2^-24        in [0, 1)
     stream 1: bonus exponentials  E[b, i]     -> E = -log(((w >> 8) + 1) * 2^-24)  in [0, 16.64]
+    stream 2: sampler exponentials E[b, i]    -> same transform (``sample``, the draw of
+              ``nanovllm/layers/sampler.py:11`` and ``draft_proposer.py:509``)
 
 ``log`` here is a fixed sequence of correctly rounded float32 operations (no
 fused multiply-add), so numpy and CUDA (``__fadd_rn``/``__fmul_rn``/
@@ -37,6 +40,7 @@ MASK32 = np.uint64(0xFFFFFFFF)
 
 STREAM_UNIFORM = 0
 STREAM_EXPONENTIAL = 1
+STREAM_SAMPLE = 2
 
 
 def philox4x32_10(c0, c1, c2, c3, k0, k1):
@@ -127,7 +131,9 @@ def uniforms(seed: int, offset: int, B: int, k: int) -> np.ndarray:
     return words_to_uniform(philox_words(seed, offset, STREAM_UNIFORM, B, k))
 
 
-def exponentials(seed: int, offset: int, B: int, V: int) -> np.ndarray:
-    """Exp(1) noise E[b, i] (the draw of ``verify.py:209``) before its clamp_min."""
-    u = words_to_open_uniform(philox_words(seed, offset, STREAM_EXPONENTIAL, B, V))
+def exponentials(seed: int, offset: int, B: int, V: int, stream: int | None = None) -> np.ndarray:
+    """Exp(1) noise E[b, i] before its clamp_min: by default stream 1, the draw of
+    ``verify.py:209``; ``STREAM_SAMPLE`` gives the sampler's draw (``sampler.py:11``)."""
+    st = STREAM_EXPONENTIAL if stream is None else stream
+    u = words_to_open_uniform(philox_words(seed, offset, st, B, V))
     return (-log_f32(u)).astype(np.float32)

@@ -9,6 +9,7 @@ CUDA kernels.  Public surface, mirroring the reference's call signatures:
   ``paged_decode_attention_cuda``, ``flash_attn_with_kvcache``,
   ``flash_attn_varlen_func``, ``store_kvcache``
 * ``verify``: ``verify_batch`` -> ``VerifyResult``
+* ``sampler``: ``Sampler``, ``sample``, ``draft_sample_step``
 * ``quant``: ``int8_linear``, ``quantize_weight``, ``dequantize_weight``
 * ``partition``: sequence sharding and tensor-parallel head sharding
 * ``context``: ``Context`` / ``set_context`` / ``get_context`` / ``reset_context``
@@ -20,6 +21,7 @@ from .attention import (Attention, flash_attn_varlen_func, flash_attn_with_kvcac
                         paged_decode_attention_cuda, store_kvcache)
 from .context import Context, get_context, reset_context, set_context  # noqa: F401
 from .quant import dequantize_weight, int8_linear, quantize_weight  # noqa: F401
+from .sampler import Sampler, draft_sample_step, sample  # noqa: F401
 from .verify import VerifyResult, verify_batch  # noqa: F401
 
 LIB_PATH = _lib.LIB_PATH

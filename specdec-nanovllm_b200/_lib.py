@@ -78,6 +78,10 @@ SIGNATURES = {
         _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_u64, _c_u64, _c_i32, _c_p, _c_p, _c_p,
         _c_i32, _c_i32, _c_i32, _c_i32, _c_p, _c_sz, _c_p]),
     "sdb_philox_fill": (_c_i32, [_c_p, _c_i32, _c_i32, _c_u64, _c_u64, _c_i32, _c_p]),
+    "sdb_sample_workspace_size": (_c_sz, [_c_i32, _c_i32]),
+    "sdb_sample": (_c_i32, [
+        _c_p, _c_i64, _c_i32, _c_p, _c_p, _c_u64, _c_u64, _c_p, _c_i64, _c_p, _c_i64, _c_i32, _c_i32,
+        _c_p, _c_sz, _c_p]),
     "sdb_w8a16_workspace_size": (_c_sz, [_c_i32] * 3),
     "sdb_w8a16_linear": (_c_i32, [
         _c_p, _c_i64, _c_p, _c_p, _c_i32, _c_i32, _c_p, _c_p, _c_i64, _c_i32, _c_i32, _c_i32,

@@ -27,9 +27,12 @@
 #include <type_traits>
 
 #include "common.cuh"
+#include "philox.cuh"
 
 namespace sdb {
 namespace vs {
+
+using namespace rng;
 
 constexpr int THREADS = 256;
 constexpr int EPT = 32;                    // logits per thread held in registers (pass 1)
@@ -65,62 +68,6 @@ struct Params {
     struct Decision* dec;  // [B]
     int* err;
 };
-
-// ------------------------------------------------------------------ Philox
-SDB_DEV void philox(uint32_t c[4], uint32_t k0, uint32_t k1) {
-#pragma unroll
-    for (int r = 0; r < 10; ++r) {
-        const uint32_t lo0 = 0xD2511F53u * c[0];
-        const uint32_t hi0 = __umulhi(0xD2511F53u, c[0]);
-        const uint32_t lo1 = 0xCD9E8D57u * c[2];
-        const uint32_t hi1 = __umulhi(0xCD9E8D57u, c[2]);
-        const uint32_t n0 = hi1 ^ c[1] ^ k0;
-        const uint32_t n2 = hi0 ^ c[3] ^ k1;
-        c[0] = n0;
-        c[1] = lo1;
-        c[2] = n2;
-        c[3] = lo0;
-        k0 += 0x9E3779B9u;
-        k1 += 0xBB67AE85u;
-    }
-}
-
-SDB_DEV uint32_t philox_word(uint32_t seed_lo, uint32_t seed_hi, uint32_t offset, uint32_t stream,
-                             uint32_t row, uint32_t col) {
-    uint32_t c[4] = {col >> 2, row, stream, offset};
-    philox(c, seed_lo, seed_hi);
-    return c[col & 3];
-}
-
-SDB_DEV float word_to_uniform(uint32_t w) { return __fmul_rn((float)(w >> 8), 5.9604644775390625e-08f); }
-SDB_DEV float word_to_open_uniform(uint32_t w) {
-    return __fmul_rn((float)((w >> 8) + 1u), 5.9604644775390625e-08f);
-}
-
-// Natural log of a positive normal float by fixed float32 operations (the atanh
-// series of log m on m in [sqrt(1/2), sqrt(2)) plus e*ln2 split in hi/lo).
-// Constants are given by bit pattern so host and device agree on every bit.
-SDB_DEV float log_fixed(float x) {
-    const uint32_t bits = __float_as_uint(x);
-    int e = (int)((bits >> 23) & 0xFFu) - 127;
-    float m = __uint_as_float((bits & 0x7FFFFFu) | 0x3F800000u);
-    if (m > __uint_as_float(0x3FB504F3u)) {  // sqrt(2)
-        m = __fmul_rn(m, 0.5f);
-        e += 1;
-    }
-    const float s = __fdiv_rn(__fsub_rn(m, 1.0f), __fadd_rn(m, 1.0f));
-    const float z = __fmul_rn(s, s);
-    float r = __uint_as_float(0x3DBA2E8Cu);                          // 1/11
-    r = __fadd_rn(__fmul_rn(r, z), __uint_as_float(0x3DE38E39u));   // 1/9
-    r = __fadd_rn(__fmul_rn(r, z), __uint_as_float(0x3E124925u));   // 1/7
-    r = __fadd_rn(__fmul_rn(r, z), __uint_as_float(0x3E4CCCCDu));   // 1/5
-    r = __fadd_rn(__fmul_rn(r, z), __uint_as_float(0x3EAAAAABu));   // 1/3
-    r = __fadd_rn(__fmul_rn(r, z), 1.0f);
-    const float lm = __fmul_rn(__fadd_rn(s, s), r);
-    const float ef = (float)e;
-    const float ln2_hi = __uint_as_float(0x3F317200u), ln2_lo = __uint_as_float(0x35BFBE8Eu);
-    return __fadd_rn(__fmul_rn(ef, ln2_hi), __fadd_rn(lm, __fmul_rn(ef, ln2_lo)));
-}
 
 SDB_DEV float accept_uniform(const Params& p, int b, int j) {
     if (p.u) return p.u[b * p.k + j];
@@ -836,7 +783,7 @@ extern "C" int sdb_verify_batch(const float* draft, const float* target, const i
 
 extern "C" int sdb_philox_fill(float* out, int rows, int cols, uint64_t seed, uint64_t offset, int stream_id,
                                void* stream) {
-    if (!out || rows <= 0 || cols <= 0 || (stream_id != 0 && stream_id != 1)) {
+    if (!out || rows <= 0 || cols <= 0 || stream_id < 0 || stream_id > 2) {
         set_last_error("bad arguments to sdb_philox_fill");
         return SDB_ERR_INVALID_ARG;
     }

@@ -11,6 +11,8 @@ own tests do, ``tests/test_spec_decode.py:14-26``), bypassing the package
 * ``nanovllm/kernels/paged_decode_attn.py`` -> ``paged_decode_attention_ref`` (:472)
 * ``nanovllm/layers/quant.py``              -> ``quantize_weight`` / ``dequantize_weight`` (:123, :151)
 * ``nanovllm/spec_decode/verify.py``        -> ``verify_batch`` (:42)
+* ``nanovllm/layers/sampler.py``            -> ``Sampler`` (:6-12), its ``torch.compile``
+  decorator replaced by the identity while the module loads
 
 ``paged_decode_attn.py`` and ``quant.py`` import triton at module level; the
 Triton kernels are only defined there (``@triton.jit`` does not need a GPU), never
@@ -212,6 +214,52 @@ def verify_cases(ref, out_dir):
         np.savez_compressed(os.path.join(out_dir, f"verify_{name}.npz"), **c)
 
 
+def sampler_cases(ref, out_dir):
+    """Sampler.forward (nanovllm/layers/sampler.py:8-12) with its exponential draw injected."""
+    sampler = ref["sampler"].Sampler()
+    g = torch.Generator().manual_seed(23)
+    cases = {}
+
+    def run(name, logits, temps, seed, e=None):
+        B, V = logits.shape
+        if e is None:
+            e = torch.from_numpy(philox.exponentials(seed, 0, B, V, stream=philox.STREAM_SAMPLE))
+        with injected_draws(torch.zeros(0), e):
+            # on fp32 logits the reference divides its argument in place (.float() is a
+            # no-op there, then div_), so it gets a copy
+            tok = sampler.forward(logits.clone(), temps)
+        is_bf16 = logits.dtype == torch.bfloat16
+        cases[name] = dict(logits=bf16_bits(logits) if is_bf16 else logits.numpy(), is_bf16=np.bool_(is_bf16),
+                           temps=temps.numpy(), seed=np.int64(seed), e=e.numpy(), tokens=tok.numpy())
+
+    run("random", torch.randn(6, 997, generator=g) * 3.0,
+        torch.tensor([1.0, 0.5, 2.0, 0.7, 1.0, 1.3]), seed=31)
+    # bf16 logits as the LM head emits them (logits.float() in the reference), 3 chunks of 8192
+    run("bf16_chunks", (torch.randn(2, 24576, generator=g) * 4.0).to(torch.bfloat16),
+        torch.tensor([0.8, 1.0]), seed=32)
+    # a vocabulary that is not a multiple of 8 (the kernel's scalar path)
+    run("ragged_vocab", torch.randn(2, 16389, generator=g) * 2.0, torch.ones(2), seed=33)
+    # one dominant logit per row
+    pk = torch.randn(4, 512, generator=g)
+    pk[torch.arange(4), torch.tensor([3, 100, 511, 0])] += 25.0
+    run("peaked", pk, torch.ones(4), seed=34)
+    # exact ties everywhere: constant logits and constant noise -> first index
+    run("ties", torch.zeros(2, 9000), torch.ones(2), seed=35, e=torch.ones(2, 9000))
+    for name, c in cases.items():
+        np.savez_compressed(os.path.join(out_dir, f"sampler_{name}.npz"), **c)
+
+
+def _load_sampler(root):
+    """layers/sampler.py decorates forward with torch.compile; load it with the decorator
+    as the identity so the plain eager ops run on CPU."""
+    real = torch.compile
+    torch.compile = lambda fn=None, **kw: fn if fn is not None else (lambda f: f)
+    try:
+        return _load(root, "ref_sampler", "nanovllm/layers/sampler.py")
+    finally:
+        torch.compile = real
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("SPECDEC_REFERENCE", "/root/reference"))
@@ -221,11 +269,13 @@ def main():
         "attn": _load(a.reference, "ref_paged_decode_attn", "nanovllm/kernels/paged_decode_attn.py"),
         "quant": _load(a.reference, "ref_quant", "nanovllm/layers/quant.py"),
         "verify": _load(a.reference, "ref_verify", "nanovllm/spec_decode/verify.py"),
+        "sampler": _load_sampler(a.reference),
     }
     torch.manual_seed(0)
     attention_cases(ref, a.out)
     quant_cases(ref, a.out)
     verify_cases(ref, a.out)
+    sampler_cases(ref, a.out)
     print("golden fixtures written to", a.out)
 
 

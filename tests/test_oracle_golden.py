@@ -79,3 +79,16 @@ def test_fixture_draws_are_the_philox_streams(golden):
     seed = int(g["seed"])
     assert np.array_equal(philox.uniforms(seed, 0, B, k), g["u"])
     assert np.array_equal(philox.exponentials(seed, 0, B, V), g["e"])
+
+
+@pytest.mark.parametrize("name", ["random", "bf16_chunks", "ragged_vocab", "peaked", "ties"])
+def test_sampler_matches_reference(golden, name):
+    """oracle.sampler against the reference's Sampler.forward with the same injected noise."""
+    from oracle import sampler as osm
+    g = golden(f"sampler_{name}")
+    logits = bf16_bits_to_f32(g["logits"]) if bool(g["is_bf16"]) else g["logits"]
+    tok = osm.sample(logits, g["temps"], exponentials=g["e"])
+    assert np.array_equal(tok, g["tokens"])
+    if name != "ties":  # the stored noise is the sampler's Philox stream
+        e = philox.exponentials(int(g["seed"]), 0, *logits.shape, stream=philox.STREAM_SAMPLE)
+        assert np.array_equal(e.view(np.uint32), g["e"].view(np.uint32))
