@@ -189,6 +189,41 @@ int sdb_paged_attention_store(const void* q, int64_t q_stride_row, int64_t q_str
                               float softmax_scale, int dtype, int splits,
                               void* workspace, size_t workspace_bytes, void* stream);
 
+/* Attention prologue of a Qwen3 layer in one launch: split of the fused QKV
+ * projection output, per-head RMSNorm of q and k, rotary embedding of q and k,
+ * and the store of the step's k / v rows into the paged cache.
+ * Replaces Qwen3Attention.forward :78-85 (split, q_norm, k_norm, rotary_emb)
+ *   nanovllm/models/qwen3.py:77-86, RMSNorm.rms_forward nanovllm/layers/layernorm.py:16-25,
+ *   RotaryEmbedding.forward / apply_rotary_emb nanovllm/layers/rotary_embedding.py:6-14, 38-50,
+ * and the store_kvcache of Attention.forward (attention.py:59-63).
+ *   qkv           (T, (Hq + 2 Hkv) D) rows qkv_stride_tok apart: q heads, k heads, v heads
+ *   q_norm_weight, k_norm_weight  (D) in the model dtype, or NULL (models with a qkv
+ *                 bias have no q/k norm, qwen3.py:68-70)
+ *   cos_sin_cache (max_position, D) float32 rows cos_sin_stride_pos apart,
+ *                 [cos(D/2) | sin(D/2)] (the RotaryEmbedding buffer)
+ *   positions     (T) int64
+ *   q_out         (T, Hq, D) normalised and rotated q
+ *   k_out, v_out  NULL or (T, Hkv, D): the normalised, rotated k and the v rows
+ *   k_cache, v_cache, slot_mapping: the paged caches and (T) int32 slots (-1 skips a
+ *                 row); slot_mapping NULL stores nothing
+ * Numerics follow the reference's eager torch: RMSNorm in float32 with 1/sqrt, the
+ * normalised value rounded to the model dtype before the weight multiply; rotary
+ * products and sums rounded separately, then rounded to the model dtype.
+ * dtype: SDB_BF16 / SDB_F16 / SDB_F32; D in {64, 128, 256}.  workspace: the
+ * attention workspace (its error word records slots past num_blocks and positions
+ * outside [0, max_position)). */
+int sdb_qk_norm_rope_store(const void* qkv, int64_t qkv_stride_tok,
+                           const void* q_norm_weight, const void* k_norm_weight, float eps,
+                           const float* cos_sin_cache, int64_t cos_sin_stride_pos, int max_position,
+                           const int64_t* positions,
+                           void* q_out, int64_t q_stride_tok, int64_t q_stride_head,
+                           void* k_out, void* v_out, int64_t kv_stride_tok, int64_t kv_stride_head,
+                           void* k_cache, void* v_cache,
+                           int64_t kv_stride_block, int64_t kv_stride_page, int64_t kv_stride_head_cache,
+                           const int32_t* slot_mapping,
+                           int T, int Hq, int Hkv, int D, int page, int num_blocks,
+                           int dtype, void* workspace, void* stream);
+
 /* =========================================================================
  * verify_batch: lossless rejection sampling of k drafted tokens.
  *

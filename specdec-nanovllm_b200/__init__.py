@@ -10,6 +10,8 @@ CUDA kernels.  Public surface, mirroring the reference's call signatures:
   ``flash_attn_varlen_func``, ``store_kvcache``
 * ``verify``: ``verify_batch`` -> ``VerifyResult``
 * ``sampler``: ``Sampler``, ``sample``, ``draft_sample_step``
+* ``prologue``: ``qk_norm_rope_store`` (split + q/k RMSNorm + rotary + KV store),
+  ``rope_cos_sin_cache``
 * ``quant``: ``int8_linear``, ``quantize_weight``, ``dequantize_weight``
 * ``partition``: sequence sharding and tensor-parallel head sharding
 * ``context``: ``Context`` / ``set_context`` / ``get_context`` / ``reset_context``
@@ -21,6 +23,7 @@ from .attention import (Attention, flash_attn_varlen_func, flash_attn_with_kvcac
                         paged_decode_attention_cuda, store_kvcache)
 from .context import Context, get_context, reset_context, set_context  # noqa: F401
 from .quant import dequantize_weight, int8_linear, quantize_weight  # noqa: F401
+from .prologue import qk_norm_rope_store, rope_cos_sin_cache  # noqa: F401
 from .sampler import Sampler, draft_sample_step, sample  # noqa: F401
 from .verify import VerifyResult, verify_batch  # noqa: F401
 

@@ -78,6 +78,10 @@ SIGNATURES = {
         _c_p, _c_p, _c_p, _c_p, _c_p, _c_p, _c_u64, _c_u64, _c_i32, _c_p, _c_p, _c_p,
         _c_i32, _c_i32, _c_i32, _c_i32, _c_p, _c_sz, _c_p]),
     "sdb_philox_fill": (_c_i32, [_c_p, _c_i32, _c_i32, _c_u64, _c_u64, _c_i32, _c_p]),
+    "sdb_qk_norm_rope_store": (_c_i32, [
+        _c_p, _c_i64, _c_p, _c_p, _c_f32, _c_p, _c_i64, _c_i32, _c_p,
+        _c_p, _c_i64, _c_i64, _c_p, _c_p, _c_i64, _c_i64, _c_p, _c_p, _c_i64, _c_i64, _c_i64, _c_p,
+        _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_p, _c_p]),
     "sdb_sample_workspace_size": (_c_sz, [_c_i32, _c_i32]),
     "sdb_sample": (_c_i32, [
         _c_p, _c_i64, _c_i32, _c_p, _c_p, _c_u64, _c_u64, _c_p, _c_i64, _c_p, _c_i64, _c_i32, _c_i32,

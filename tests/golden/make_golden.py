@@ -11,8 +11,12 @@ own tests do, ``tests/test_spec_decode.py:14-26``), bypassing the package
 * ``nanovllm/kernels/paged_decode_attn.py`` -> ``paged_decode_attention_ref`` (:472)
 * ``nanovllm/layers/quant.py``              -> ``quantize_weight`` / ``dequantize_weight`` (:123, :151)
 * ``nanovllm/spec_decode/verify.py``        -> ``verify_batch`` (:42)
-* ``nanovllm/layers/sampler.py``            -> ``Sampler`` (:6-12), its ``torch.compile``
-  decorator replaced by the identity while the module loads
+* ``nanovllm/layers/sampler.py``            -> ``Sampler`` (:6-12)
+* ``nanovllm/layers/layernorm.py``          -> ``RMSNorm`` (:6-44)
+* ``nanovllm/layers/rotary_embedding.py``   -> ``RotaryEmbedding`` (:17-50)
+
+(the last three with their ``torch.compile`` decorators replaced by the identity while
+the module loads, so the eager ops run on CPU)
 
 ``paged_decode_attn.py`` and ``quant.py`` import triton at module level; the
 Triton kernels are only defined there (``@triton.jit`` does not need a GPU), never
@@ -249,6 +253,50 @@ def sampler_cases(ref, out_dir):
         np.savez_compressed(os.path.join(out_dir, f"sampler_{name}.npz"), **c)
 
 
+def prologue_cases(ref, out_dir):
+    """q_norm / k_norm (RMSNorm.rms_forward, layernorm.py:16-25) and rotary_emb
+    (RotaryEmbedding.forward, rotary_embedding.py:38-50) as qwen3.py:77-85 applies them,
+    bf16 on CPU."""
+    g = torch.Generator().manual_seed(29)
+    T, Hq, Hkv, D = 12, 8, 2, 128
+    qkv = (torch.randn(T, (Hq + 2 * Hkv) * D, generator=g) * 2.0).to(torch.bfloat16)
+    positions = torch.tensor([0, 1, 7, 300, 4095, 4096, 17, 1000, 2047, 5, 63, 64])
+    q_norm = ref["layernorm"].RMSNorm(D, eps=1e-6)
+    k_norm = ref["layernorm"].RMSNorm(D, eps=1e-6)
+    with torch.no_grad():
+        q_norm.weight.copy_(torch.rand(D, generator=g) * 2.0)
+        k_norm.weight.copy_(torch.rand(D, generator=g) * 2.0)
+    q_norm = q_norm.to(torch.bfloat16)
+    k_norm = k_norm.to(torch.bfloat16)
+    rope = ref["rope"].RotaryEmbedding(D, D, 8192, 1000000.0)
+    q, k, v = qkv.split([Hq * D, Hkv * D, Hkv * D], dim=-1)
+    q = q.reshape(-1, Hq, D)
+    k = k.reshape(-1, Hkv, D)
+    v = v.reshape(-1, Hkv, D)
+    with torch.no_grad():
+        qn = q_norm(q)
+        kn = k_norm(k)
+        qr, kr = rope(positions, qn, kn)
+    np.savez_compressed(os.path.join(out_dir, "prologue_qwen3.npz"),
+                        qkv=bf16_bits(qkv), positions=positions.numpy(),
+                        q_norm_w=bf16_bits(q_norm.weight.data), k_norm_w=bf16_bits(k_norm.weight.data),
+                        eps=np.float32(1e-6), rope_base=np.float64(1000000.0), max_position=np.int64(8192),
+                        cos_sin_rows=rope.cos_sin_cache.squeeze(1)[positions].numpy(),
+                        q=bf16_bits(qr), k=bf16_bits(kr), v=bf16_bits(v), Hq=np.int64(Hq),
+                        Hkv=np.int64(Hkv), D=np.int64(D))
+
+
+def _load_compiled(root, name, rel):
+    """Load a reference module whose methods carry torch.compile, with the decorator as
+    the identity so the plain eager ops run on CPU."""
+    real = torch.compile
+    torch.compile = lambda fn=None, **kw: fn if fn is not None else (lambda f: f)
+    try:
+        return _load(root, name, rel)
+    finally:
+        torch.compile = real
+
+
 def _load_sampler(root):
     """layers/sampler.py decorates forward with torch.compile; load it with the decorator
     as the identity so the plain eager ops run on CPU."""
@@ -270,12 +318,15 @@ def main():
         "quant": _load(a.reference, "ref_quant", "nanovllm/layers/quant.py"),
         "verify": _load(a.reference, "ref_verify", "nanovllm/spec_decode/verify.py"),
         "sampler": _load_sampler(a.reference),
+        "layernorm": _load_compiled(a.reference, "ref_layernorm", "nanovllm/layers/layernorm.py"),
+        "rope": _load_compiled(a.reference, "ref_rope", "nanovllm/layers/rotary_embedding.py"),
     }
     torch.manual_seed(0)
     attention_cases(ref, a.out)
     quant_cases(ref, a.out)
     verify_cases(ref, a.out)
     sampler_cases(ref, a.out)
+    prologue_cases(ref, a.out)
     print("golden fixtures written to", a.out)
 
 

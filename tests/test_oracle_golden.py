@@ -92,3 +92,30 @@ def test_sampler_matches_reference(golden, name):
     if name != "ties":  # the stored noise is the sampler's Philox stream
         e = philox.exponentials(int(g["seed"]), 0, *logits.shape, stream=philox.STREAM_SAMPLE)
         assert np.array_equal(e.view(np.uint32), g["e"].view(np.uint32))
+
+
+def test_prologue_matches_reference(golden):
+    """oracle.prologue against the reference's RMSNorm + RotaryEmbedding (qwen3.py:82-85)."""
+    from oracle import prologue as op
+    g = golden("prologue_qwen3")
+    Hq, Hkv, D = int(g["Hq"]), int(g["Hkv"]), int(g["D"])
+    qkv = bf16_bits_to_f32(g["qkv"])
+    T = qkv.shape[0]
+    # a table holding only the rows the positions use (anything else would be NaN)
+    cs = np.full((int(g["max_position"]), D), np.nan, dtype=np.float32)
+    cs[g["positions"]] = g["cos_sin_rows"]
+    q, k, v = op.qk_prologue(qkv, g["positions"], Hq, Hkv, D, cs, bf16_bits_to_f32(g["q_norm_w"]),
+                             bf16_bits_to_f32(g["k_norm_w"]), float(g["eps"]), "bf16")
+    for got, key in ((q, "q"), (k, "k"), (v, "v")):
+        want = bf16_bits_to_f32(g[key]).reshape(got.shape)
+        # the mean of squares is summed in another order than torch's: at most one
+        # bf16 ulp apart, on a small fraction of the elements
+        ok, err, _ = allclose_report(got, want, rtol=1e-2, atol=1e-3)
+        assert ok, (key, err)
+        assert np.mean(got == want) > 0.98, key
+
+
+def test_rope_table_matches_reference(golden, pkg):
+    g = golden("prologue_qwen3")
+    cs = pkg.rope_cos_sin_cache(int(g["D"]), int(g["max_position"]), float(g["rope_base"]), device="cpu")
+    assert np.array_equal(cs.numpy()[g["positions"]].view(np.uint32), g["cos_sin_rows"].view(np.uint32))
