@@ -252,6 +252,21 @@ int sdb_verify_batch(const float* draft_logits, const float* target_logits,
                      int B, int k, int target_rows, int V,
                      void* workspace, size_t workspace_bytes, void* stream);
 
+/* verify_batch with logits of any float type, read as float32 exactly in the kernels
+ * (the reference converts with .float(), verify.py:194): the engine passes the
+ * LM head's bf16 target logits straight in (model_runner.py:1101-1103), so no
+ * (B, k+1, V) float32 copy is made.  draft_dtype / target_dtype: SDB_F32,
+ * SDB_BF16 or SDB_F16; everything else as sdb_verify_batch (which is this call
+ * with both SDB_F32). */
+int sdb_verify_batch_ex(const void* draft_logits, int draft_dtype,
+                        const void* target_logits, int target_dtype,
+                        const int64_t* draft_tokens, const float* temperatures,
+                        const float* uniforms, const float* exponentials,
+                        uint64_t seed, uint64_t offset, int draft_is_point_mass,
+                        int64_t* out_accepted, int64_t* out_bonus, uint8_t* out_accept_mask,
+                        int B, int k, int target_rows, int V,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
 /* Philox streams of the samplers written out (test and debugging aid): stream 0
  * as uniforms [rows, cols], stream 1 (verify_batch) or 2 (sample) as
  * exponentials [rows, cols]. */

@@ -49,8 +49,10 @@ constexpr int BS_THREADS = 32 * (BS_CONSUMERS + 1);
 constexpr int BS_SMEM = BS_STAGES * CHUNK1 * 4;
 
 struct Params {
-    const float* draft;    // (B, k, V)
-    const float* target;   // (B, Tr, V)
+    const void* draft;     // (B, k, V)
+    const void* target;    // (B, Tr, V)
+    int dkind, tkind;      // element type of draft / target: 0 float32, 1 bfloat16, 2 float16
+    int vec;               // passes 3-4 read rows in 16-byte vectors (group_col layout)
     const int64_t* tokens; // (B, k)
     const float* temps;    // (B) or null
     const float* u;        // (B, k) or null
@@ -76,6 +78,60 @@ SDB_DEV float accept_uniform(const Params& p, int b, int j) {
 
 // x / T exactly as torch divides (IEEE); T == 1 is the identity.
 SDB_DEV float scale_t(float x, float T) { return T == 1.0f ? x : __fdiv_rn(x, T); }
+
+// One row of logits of any of the three element types, read as float32 exactly (the
+// reference converts with .float(), verify.py:194).  The type is uniform per call,
+// so the branches below never diverge.
+SDB_DEV float half_bits_to_f32(uint32_t h, int kind) {
+    return kind == 1 ? __uint_as_float(h << 16) : __half2float(__ushort_as_half((unsigned short)h));
+}
+// Two packed 16-bit logits -> float32 (kind 1 bfloat16, 2 float16), one branch per pair.
+SDB_DEV float2 unpack2(uint32_t u, int kind) {
+    if (kind == 1) return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
+    return __half22float2(*reinterpret_cast<const __half2*>(&u));
+}
+struct Row {
+    const uint8_t* p;  // null: no row
+    int kind;
+    SDB_DEV float at(int64_t i) const {
+        if (kind == 0) return __ldg(reinterpret_cast<const float*>(p) + i);
+        return half_bits_to_f32(__ldg(reinterpret_cast<const unsigned short*>(p) + i), kind);
+    }
+    // four logits from i (i % 4 == 0; rows 8-byte aligned for 16-bit types)
+    SDB_DEV float4 at4(int64_t i) const {
+        if (kind == 0) return __ldg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p) + i));
+        const uint2 u = __ldg(reinterpret_cast<const uint2*>(reinterpret_cast<const unsigned short*>(p) + i));
+        const float2 a = unpack2(u.x, kind), b = unpack2(u.y, kind);
+        return make_float4(a.x, a.y, b.x, b.y);
+    }
+    // eight logits from i (i % 8 == 0), in two groups of four: one 16-byte load for
+    // 16-bit rows (16-byte aligned: V % 8 == 0), two for float32 rows; `left` logits
+    // of the row remain from i (a float32 row may end after the first group)
+    SDB_DEV void at8(int64_t i, int left, float4& g0, float4& g1) const {
+        if (kind == 0) {
+            const float4* q = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p) + i);
+            g0 = __ldg(q);
+            if (left > 4) g1 = __ldg(q + 1);
+            return;
+        }
+        const uint4 u = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const unsigned short*>(p) + i));
+        const float2 a = unpack2(u.x, kind), b = unpack2(u.y, kind), c = unpack2(u.z, kind), d = unpack2(u.w, kind);
+        g0 = make_float4(a.x, a.y, b.x, b.y);
+        g1 = make_float4(c.x, c.y, d.x, d.y);
+    }
+};
+
+// Column of group q (four consecutive logits) of this thread in the vector form of
+// passes 3-4: pairs of groups are adjacent, so one 16-byte load covers a pair of
+// 16-bit groups.
+SDB_DEV int group_col(int q) { return (q >> 1) * THREADS * 8 + (int)threadIdx.x * 8 + (q & 1) * 4; }
+SDB_DEV int elem_bytes(int kind) { return kind == 0 ? 4 : 2; }
+SDB_DEV Row draft_row(const Params& p, int64_t row) {
+    return Row{reinterpret_cast<const uint8_t*>(p.draft) + row * p.V * elem_bytes(p.dkind), p.dkind};
+}
+SDB_DEV Row target_row(const Params& p, int64_t row) {
+    return Row{reinterpret_cast<const uint8_t*>(p.target) + row * p.V * elem_bytes(p.tkind), p.tkind};
+}
 
 // ------------------------------------------------------------------ reductions
 template <typename F>
@@ -107,13 +163,13 @@ __global__ void __launch_bounds__(THREADS, 4) vs_row_stats(const Params p) {
     // point-mass drafts need no statistics: the grid then starts at the target rows
     const int row = blockIdx.x + (p.point_mass ? nd : 0);
     const int c = blockIdx.y;
-    const float* src;
+    Row src;
     int b;
     if (row < nd) {
-        src = p.draft + (int64_t)row * p.V;
+        src = draft_row(p, row);
         b = row / p.k;
     } else {
-        src = p.target + (int64_t)(row - nd) * p.V;
+        src = target_row(p, row - nd);
         b = (row - nd) / p.Tr;
     }
     const float T = p.temps ? p.temps[b] : 1.0f;
@@ -125,7 +181,7 @@ __global__ void __launch_bounds__(THREADS, 4) vs_row_stats(const Params p) {
         for (int it = 0; it < EPT / 4; ++it) {
             const int idx = it * THREADS * 4 + threadIdx.x * 4;
             float4 x = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-            if (idx < n) x = __ldcs(reinterpret_cast<const float4*>(src + base + idx));
+            if (idx < n) x = src.at4(base + idx);
             v[it * 4 + 0] = idx < n ? x.x : -INFINITY;
             v[it * 4 + 1] = idx < n ? x.y : -INFINITY;
             v[it * 4 + 2] = idx < n ? x.z : -INFINITY;
@@ -135,7 +191,7 @@ __global__ void __launch_bounds__(THREADS, 4) vs_row_stats(const Params p) {
 #pragma unroll
         for (int it = 0; it < EPT; ++it) {
             const int idx = it * THREADS + threadIdx.x;
-            v[it] = idx < n ? __ldcs(src + base + idx) : -INFINITY;
+            v[it] = idx < n ? src.at(base + idx) : -INFINITY;
         }
     }
     if (T != 1.0f) {  // x / T as torch divides (IEEE), one uniform branch per CTA
@@ -162,19 +218,24 @@ __global__ void __launch_bounds__(THREADS, 4) vs_row_stats(const Params p) {
 // Pass 1 for 16-byte-aligned rows with V % 4 == 0: items (row, chunk) strided over
 // persistent CTAs; the last warp streams each item's 32 KB into the stage ring with one
 // bulk copy, the consumer warps reduce it from shared memory and release the stage.
-SDB_DEV const float* logits_row(const Params& p, int row, int& b) {
+SDB_DEV Row logits_row(const Params& p, int row, int& b) {
     const int nd = p.B * p.k;
     if (row < nd) {
         b = row / p.k;
-        return p.draft + (int64_t)row * p.V;
+        return draft_row(p, row);
     }
     b = (row - nd) / p.Tr;
-    return p.target + (int64_t)(row - nd) * p.V;
+    return target_row(p, row - nd);
 }
 
 __global__ void __launch_bounds__(BS_THREADS, 2) vs_row_stats_bulk(const Params p, int row0, int nrows) {
     extern __shared__ __align__(128) uint8_t ring[];
     __shared__ __align__(8) uint64_t bars[2 * BS_STAGES];
+    // per stage, written by the producer before it arms the stage: the item's row and
+    // chunk, its logit count and element type, and the row's temperature, so the
+    // consumers do no index arithmetic (integer divisions) per item
+    __shared__ int meta_row[BS_STAGES], meta_c[BS_STAGES], meta_n[BS_STAGES], meta_kind[BS_STAGES];
+    __shared__ float meta_t[BS_STAGES];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int total = nrows * p.C1;
     const uint32_t full0 = smem_u32(bars), empty0 = full0 + 8 * BS_STAGES;
@@ -197,10 +258,18 @@ __global__ void __launch_bounds__(BS_THREADS, 2) vs_row_stats_bulk(const Params 
                     break;
                 }
                 int b;
-                const int c = it % p.C1;
-                const float* src = logits_row(p, row0 + it / p.C1, b) + c * CHUNK1;
-                const uint32_t bytes = 4u * (uint32_t)min(CHUNK1, p.V - c * CHUNK1);
-                mbar_arrive_expect_tx(full0 + 8 * s, bytes);
+                const int c = it % p.C1, row = row0 + it / p.C1;
+                const Row r = logits_row(p, row, b);
+                const int esz = elem_bytes(r.kind);
+                const uint8_t* src = r.p + (int64_t)c * CHUNK1 * esz;
+                const int n = min(CHUNK1, p.V - c * CHUNK1);
+                const uint32_t bytes = (uint32_t)esz * (uint32_t)n;
+                meta_row[s] = row;
+                meta_c[s] = c;
+                meta_n[s] = n;
+                meta_kind[s] = r.kind;
+                meta_t[s] = p.temps ? p.temps[b] : 1.0f;
+                mbar_arrive_expect_tx(full0 + 8 * s, bytes);  // release: the consumers see the metadata
                 bulk_load(smem_u32(ring + s * CHUNK1 * 4), src, bytes, full0 + 8 * s, pol);
             }
             for (int q = g - BS_STAGES > 0 ? g - BS_STAGES : 0; q < g; ++q)  // own copies land before exit
@@ -217,32 +286,56 @@ __global__ void __launch_bounds__(BS_THREADS, 2) vs_row_stats_bulk(const Params 
             ok = false;
             if (lane == 0) atomicOr(p.err, SDB_KERR_TIMEOUT);
         }
-        int b;
-        const int row = row0 + it / p.C1, c = it % p.C1;
-        logits_row(p, row, b);
-        const float T = p.temps ? p.temps[b] : 1.0f;
-        const int n = min(CHUNK1, p.V - c * CHUNK1);
-        const float4* st = reinterpret_cast<const float4*>(ring + s * CHUNK1 * 4) + warp * (CHUNK1 / 4 / SUB);
+        const int row = meta_row[s], c = meta_c[s], n = meta_n[s], kind = meta_kind[s];
+        const float T = meta_t[s];
+        // this warp's 512 logits of the chunk (the assignment of logits to lanes is free:
+        // only their max and sum are formed): float32 as 4 x 16 bytes per lane, 16-bit
+        // types as 2 x 16 bytes per lane; the type branch is uniform per item
+        const uint8_t* sb = ring + s * CHUNK1 * 4;
         float v[BS_EPT];
-        if (n == CHUNK1) {
-#pragma unroll
-            for (int q = 0; q < BS_EPT / 4; ++q) {
-                const float4 x = st[q * 32 + lane];
-                v[4 * q + 0] = x.x;
-                v[4 * q + 1] = x.y;
-                v[4 * q + 2] = x.z;
-                v[4 * q + 3] = x.w;
-            }
-        } else {  // the last chunk of a row
+        if (kind == 0) {
+            const float4* st = reinterpret_cast<const float4*>(sb) + warp * (CHUNK1 / 4 / SUB);
 #pragma unroll
             for (int q = 0; q < BS_EPT / 4; ++q) {
                 const int i4 = q * 32 + lane;
-                const float4 x = st[i4];
                 const bool in = 4 * (warp * (CHUNK1 / 4 / SUB) + i4) < n;
+                const float4 x = st[i4];
                 v[4 * q + 0] = in ? x.x : -INFINITY;
                 v[4 * q + 1] = in ? x.y : -INFINITY;
                 v[4 * q + 2] = in ? x.z : -INFINITY;
                 v[4 * q + 3] = in ? x.w : -INFINITY;
+            }
+        } else {
+            const uint4* st = reinterpret_cast<const uint4*>(sb) + warp * (CHUNK1 / 8 / SUB);
+            uint4 u[BS_EPT / 8];
+            bool in[BS_EPT / 8];
+#pragma unroll
+            for (int q = 0; q < BS_EPT / 8; ++q) {
+                const int i8 = q * 32 + lane;
+                in[q] = 8 * (warp * (CHUNK1 / 8 / SUB) + i8) < n;  // n % 8 == 0 on this path
+                u[q] = st[i8];
+            }
+            if (kind == 1) {
+#pragma unroll
+                for (int q = 0; q < BS_EPT / 8; ++q) {
+                    const uint32_t w[4] = {u[q].x, u[q].y, u[q].z, u[q].w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        v[8 * q + 2 * e] = in[q] ? __uint_as_float(w[e] << 16) : -INFINITY;
+                        v[8 * q + 2 * e + 1] = in[q] ? __uint_as_float(w[e] & 0xffff0000u) : -INFINITY;
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int q = 0; q < BS_EPT / 8; ++q) {
+                    const uint32_t w[4] = {u[q].x, u[q].y, u[q].z, u[q].w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float2 f2 = __half22float2(*reinterpret_cast<const __half2*>(&w[e]));
+                        v[8 * q + 2 * e] = in[q] ? f2.x : -INFINITY;
+                        v[8 * q + 2 * e + 1] = in[q] ? f2.y : -INFINITY;
+                    }
+                }
             }
         }
         __syncwarp();
@@ -268,7 +361,7 @@ __global__ void __launch_bounds__(BS_THREADS, 2) vs_row_stats_bulk(const Params 
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-        if (lane == 0) __stcg(p.stats + ((int64_t)row * p.C1 + c) * SUB + warp, make_float2(mx, sum));
+        if (ok && lane == 0) __stcg(p.stats + ((int64_t)row * p.C1 + c) * SUB + warp, make_float2(mx, sum));
     }
 }
 
@@ -328,10 +421,10 @@ __global__ void __launch_bounds__(DECIDE_THREADS) vs_decide(const Params p) {
             tok = 0;
         }
         const int drow = b * p.k + lane;
-        const float xq = p.draft[(int64_t)drow * p.V + tok];
+        const float xq = draft_row(p, drow).at(tok);
         const float q_tok = p.point_mass ? xq : expf(scale_t(xq, T) - sM[lane]) * sI[lane];
         const float p_tok =
-            expf(scale_t(p.target[(int64_t)(b * p.Tr + lane) * p.V + tok], T) - sM[p.k + lane]) * sI[p.k + lane];
+            expf(scale_t(target_row(p, b * p.Tr + lane).at(tok), T) - sM[p.k + lane]) * sI[p.k + lane];
         const float ratio = q_tok > 0.f ? fminf(__fdiv_rn(p_tok, fmaxf(q_tok, 1e-10f)), 1.0f) : 0.f;
         acc = accept_uniform(p, b, lane) < ratio;
         p.out_mask[b * p.k + lane] = acc ? 1 : 0;
@@ -376,39 +469,42 @@ SDB_DEV Decision load_decision(const Params& p, int b) {
 }
 
 // Row a of the target (clamped) and of the draft (none when a == k) for sequence b.
-SDB_DEV const float* target_row_a(const Params& p, int b, const Decision& d) {
-    return p.target + (int64_t)(b * p.Tr + min(d.a, p.Tr - 1)) * p.V;
+SDB_DEV Row target_row_a(const Params& p, int b, const Decision& d) {
+    return target_row(p, b * p.Tr + min(d.a, p.Tr - 1));
 }
-SDB_DEV const float* draft_row_a(const Params& p, int b, const Decision& d) {
-    return d.a < p.k ? p.draft + (int64_t)(b * p.k + d.a) * p.V : nullptr;
+SDB_DEV Row draft_row_a(const Params& p, int b, const Decision& d) {
+    return d.a < p.k ? draft_row(p, b * p.k + d.a) : Row{nullptr, p.dkind};
 }
 
 // Visits the logits of this CTA's chunk of row a as (index, target logit, draft
 // logit): float4 loads issued together when V % 4 == 0, scalar loads otherwise.
 template <typename F>
-SDB_DEV void for_chunk(const Params& p, const float* tr, const float* dr, int base, F f) {
+SDB_DEV void for_chunk(const Params& p, const Row& tr, const Row& dr, int base, F f) {
     const int n = min(CHUNK2, p.V - base);
-    if ((p.V & 3) == 0) {
+    if (p.vec) {
         float4 xt[EPT2 / 4], xd[EPT2 / 4];
 #pragma unroll
         for (int it = 0; it < EPT2 / 4; ++it) {
-            const int idx = it * THREADS * 4 + threadIdx.x * 4;
             xt[it] = make_float4(0.f, 0.f, 0.f, 0.f);
             xd[it] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int q2 = 0; q2 < EPT2 / 8; ++q2) {
+            const int idx = group_col(2 * q2);
             if (idx < n) {
-                xt[it] = __ldg(reinterpret_cast<const float4*>(tr + base + idx));
-                if (dr) xd[it] = __ldg(reinterpret_cast<const float4*>(dr + base + idx));
+                tr.at8(base + idx, n - idx, xt[2 * q2], xt[2 * q2 + 1]);
+                if (dr.p) dr.at8(base + idx, n - idx, xd[2 * q2], xd[2 * q2 + 1]);
             }
         }
 #pragma unroll
         for (int it = 0; it < EPT2 / 4; ++it) {
-            const int idx = it * THREADS * 4 + threadIdx.x * 4;
+            const int idx = group_col(it);
             if (idx < n) f(base + idx, xt[it], xd[it]);
         }
     } else {
         for (int idx = threadIdx.x; idx < n; idx += THREADS) {
-            const float4 t1 = make_float4(__ldg(tr + base + idx), 0.f, 0.f, 0.f);
-            const float4 d1 = make_float4(dr ? __ldg(dr + base + idx) : 0.f, 0.f, 0.f, 0.f);
+            const float4 t1 = make_float4(tr.at(base + idx), 0.f, 0.f, 0.f);
+            const float4 d1 = make_float4(dr.p ? dr.at(base + idx) : 0.f, 0.f, 0.f, 0.f);
             f(base + idx, t1, d1);  // only .x is meaningful: lanes of one logit
         }
     }
@@ -420,9 +516,9 @@ __global__ void __launch_bounds__(THREADS) vs_resid_sums(const Params p) {
     const int b = blockIdx.x, c = blockIdx.y;
     const Decision d = load_decision(p, b);
     const float T = p.temps ? p.temps[b] : 1.0f;
-    const float* tr = target_row_a(p, b, d);
-    const float* dr = draft_row_a(p, b, d);
-    const int cnt = (p.V & 3) == 0 ? 4 : 1;
+    const Row tr = target_row_a(p, b, d);
+    const Row dr = draft_row_a(p, b, d);
+    const int cnt = p.vec ? 4 : 1;
     float sr = 0.f, sp = 0.f;
     auto body = [&](auto unit) {
         for_chunk(p, tr, dr, c * CHUNK2, [&](int, const float4& xt, const float4& xd) {
@@ -494,8 +590,8 @@ __global__ void __launch_bounds__(THREADS) vs_bonus(const Params p) {
     const float T = p.temps ? p.temps[b] : 1.0f;
     const float Z = zsh;
     const bool up = use_p != 0;
-    const float* tr = target_row_a(p, b, d);
-    const float* dr = draft_row_a(p, b, d);
+    const Row tr = target_row_a(p, b, d);
+    const Row dr = draft_row_a(p, b, d);
     float best = -INFINITY;
     int bidx = 0x7fffffff;
     // Exact value of column i: (v / Z) / max(E, 1e-10) with v = p[a] or resid[a].
@@ -510,7 +606,7 @@ __global__ void __launch_bounds__(THREADS) vs_bonus(const Params p) {
         }
     };
     auto body = [&](auto unit) {
-        if ((p.V & 3) != 0) {
+        if (!p.vec) {
             for_chunk(p, tr, dr, c * CHUNK2, [&](int i, const float4& xt, const float4& xd) {
                 float E[4];
                 exp_noise4(p, b, i, 1, E);
@@ -518,7 +614,7 @@ __global__ void __launch_bounds__(THREADS) vs_bonus(const Params p) {
             });
             return;
         }
-        // V % 4 == 0: every lane holds 16 columns (4 runs of 4).  Cheap bounds first:
+        // vector form: every lane holds 16 columns (4 runs of 4).  Cheap bounds first:
         // v in [v_lo, v_hi] from fast exponentials (within 2^-10 of expf above
         // exponent -8192; the residual max(p - q, 0) from p_lo - q_hi and p_hi) and
         // E = max(-log U, 1e-10) in [max(1 - U, 1e-10), max((1 - U) / U, 1e-10)].  The
@@ -531,12 +627,15 @@ __global__ void __launch_bounds__(THREADS) vs_bonus(const Params p) {
         float4 xt[EPT2 / 4], xd[EPT2 / 4];
 #pragma unroll
         for (int q = 0; q < EPT2 / 4; ++q) {
-            const int idx = q * THREADS * 4 + threadIdx.x * 4;
             xt[q] = make_float4(0.f, 0.f, 0.f, 0.f);
             xd[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int q2 = 0; q2 < EPT2 / 8; ++q2) {
+            const int idx = group_col(2 * q2);
             if (idx < n) {
-                xt[q] = __ldg(reinterpret_cast<const float4*>(tr + base + idx));
-                if (dr) xd[q] = __ldg(reinterpret_cast<const float4*>(dr + base + idx));
+                tr.at8(base + idx, n - idx, xt[2 * q2], xt[2 * q2 + 1]);
+                if (dr.p) dr.at8(base + idx, n - idx, xd[2 * q2], xd[2 * q2 + 1]);
             }
         }
         constexpr float kLog2e = 1.4426950408889634f;
@@ -545,7 +644,7 @@ __global__ void __launch_bounds__(THREADS) vs_bonus(const Params p) {
         float lbmax = 0.f;
 #pragma unroll
         for (int q = 0; q < EPT2 / 4; ++q) {
-            const int idx = q * THREADS * 4 + threadIdx.x * 4;
+            const int idx = group_col(q);
             const bool in = idx < n;
             const float t4[4] = {xt[q].x, xt[q].y, xt[q].z, xt[q].w};
             const float d4[4] = {xd[q].x, xd[q].y, xd[q].z, xd[q].w};
@@ -592,12 +691,12 @@ __global__ void __launch_bounds__(THREADS) vs_bonus(const Params p) {
         while (live) {
             const int j = __ffs(live) - 1;
             live &= live - 1;
-            const int i = base + (j >> 2) * THREADS * 4 + threadIdx.x * 4 + (j & 3);
+            const int i = base + group_col(j >> 2) + (j & 3);
             const float E = p.e ? fmaxf(p.e[(int64_t)b * p.V + i], 1e-10f)
                                 : fmaxf(-log_fixed(word_to_open_uniform(philox_word(
                                             p.seed_lo, p.seed_hi, p.offset, 1u, (uint32_t)b, (uint32_t)i))),
                                         1e-10f);
-            exact(unit, i, __ldg(tr + i), dr ? __ldg(dr + i) : 0.f, E);
+            exact(unit, i, tr.at(i), dr.p ? dr.at(i) : 0.f, E);
         }
     };
     if (T == 1.0f) body(std::true_type{});
@@ -704,10 +803,11 @@ extern "C" size_t sdb_verify_workspace_size(int B, int k, int target_rows, int V
     return vs::ws_layout(B, k, target_rows, V).total;
 }
 
-extern "C" int sdb_verify_batch(const float* draft, const float* target, const int64_t* tokens, const float* temps,
-                                const float* uniforms, const float* exponentials, uint64_t seed, uint64_t offset,
-                                int point_mass, int64_t* out_acc, int64_t* out_bonus, uint8_t* out_mask, int B,
-                                int k, int Tr, int V, void* workspace, size_t workspace_bytes, void* stream) {
+extern "C" int sdb_verify_batch_ex(const void* draft, int draft_dtype, const void* target, int target_dtype,
+                                   const int64_t* tokens, const float* temps, const float* uniforms,
+                                   const float* exponentials, uint64_t seed, uint64_t offset, int point_mass,
+                                   int64_t* out_acc, int64_t* out_bonus, uint8_t* out_mask, int B, int k, int Tr,
+                                   int V, void* workspace, size_t workspace_bytes, void* stream) {
     if (!draft || !target || !tokens || !out_acc || !out_bonus || !out_mask || !workspace) {
         set_last_error("null pointer argument");
         return SDB_ERR_INVALID_ARG;
@@ -716,6 +816,12 @@ extern "C" int sdb_verify_batch(const float* draft, const float* target, const i
         set_last_error("bad sizes B=%d k=%d target_rows=%d V=%d (need B <= %d, 1<=k<=32, target_rows in {k, k+1})",
                        B, k, Tr, V, vs::kCounterCap);
         return SDB_ERR_INVALID_ARG;
+    }
+    auto kind_of = [](int dt) { return dt == SDB_F32 ? 0 : (dt == SDB_BF16 ? 1 : (dt == SDB_F16 ? 2 : -1)); };
+    const int dkind = kind_of(draft_dtype), tkind = kind_of(target_dtype);
+    if (dkind < 0 || tkind < 0) {
+        set_last_error("logits dtypes %d / %d not supported (float32, bfloat16, float16)", draft_dtype, target_dtype);
+        return SDB_ERR_UNSUPPORTED;
     }
     if ((reinterpret_cast<uintptr_t>(workspace) & 255) ||
         ((V & 3) == 0 && ((reinterpret_cast<uintptr_t>(draft) & 15) || (reinterpret_cast<uintptr_t>(target) & 15)))) {
@@ -731,6 +837,8 @@ extern "C" int sdb_verify_batch(const float* draft, const float* target, const i
     vs::Params p{};
     p.draft = draft;
     p.target = target;
+    p.dkind = dkind;
+    p.tkind = tkind;
     p.tokens = tokens;
     p.temps = temps;
     p.u = uniforms;
@@ -757,8 +865,15 @@ extern "C" int sdb_verify_batch(const float* draft, const float* target, const i
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     const int row0 = point_mass ? B * k : 0;
     const int nrows = B * ((point_mass ? 0 : k) + Tr);
+    // bulk copies need every streamed row to be a whole number of 16-byte units (the
+    // bases were checked above): V % 4 == 0 for float32 rows, V % 8 == 0 for 16-bit ones
+    // passes 3-4 read 16-byte vectors when every row they read is 16-byte aligned (the
+    // point-mass draft is read too: its residual row)
+    p.vec = (V & 3) == 0 && (dkind == 0 || (V & 7) == 0) && (tkind == 0 || (V & 7) == 0);
+    const bool draft_rows_ok = point_mass || ((V * (dkind == 0 ? 4 : 2)) % 16 == 0);
+    const bool target_rows_ok = (V * (tkind == 0 ? 4 : 2)) % 16 == 0;
     int rc;
-    if ((V & 3) == 0) {  // rows 16-byte aligned (the pointers were checked above)
+    if ((V & 3) == 0 && draft_rows_ok && target_rows_ok) {
         rc = ensure_smem_attr(reinterpret_cast<const void*>(vs::vs_row_stats_bulk), vs::BS_SMEM, 50);
         if (rc) return rc;
         const long long items = (long long)nrows * p.C1;
@@ -779,6 +894,15 @@ extern "C" int sdb_verify_batch(const float* draft, const float* target, const i
     if (rc) return rc;
     vs::vs_bonus<<<dim3(B, p.C2), vs::THREADS, 0, st>>>(p);
     return cuda_status(cudaGetLastError(), "vs_bonus launch");
+}
+
+extern "C" int sdb_verify_batch(const float* draft, const float* target, const int64_t* tokens, const float* temps,
+                                const float* uniforms, const float* exponentials, uint64_t seed, uint64_t offset,
+                                int point_mass, int64_t* out_acc, int64_t* out_bonus, uint8_t* out_mask, int B,
+                                int k, int Tr, int V, void* workspace, size_t workspace_bytes, void* stream) {
+    return sdb_verify_batch_ex(draft, SDB_F32, target, SDB_F32, tokens, temps, uniforms, exponentials, seed, offset,
+                               point_mass, out_acc, out_bonus, out_mask, B, k, Tr, V, workspace, workspace_bytes,
+                               stream);
 }
 
 extern "C" int sdb_philox_fill(float* out, int rows, int cols, uint64_t seed, uint64_t offset, int stream_id,

@@ -51,8 +51,10 @@ def verify_batch(draft_probs: torch.Tensor, target_logits: torch.Tensor, draft_t
         raise ValueError(f"target_logits {tuple(target_logits.shape)} vs draft {tuple(draft_probs.shape)}")
     if tuple(draft_tokens.shape) != (B, k):
         raise ValueError(f"draft_tokens must be ({B}, {k})")
-    draft = draft_probs.float().contiguous()
-    target = target_logits.float().contiguous()
+    # float32 / bfloat16 / float16 logits are read as they are (converted exactly in the
+    # kernels, as the reference's .float()); other types are converted here
+    draft = (draft_probs if draft_probs.dtype in _lib.DTYPE_CODE else draft_probs.float()).contiguous()
+    target = (target_logits if target_logits.dtype in _lib.DTYPE_CODE else target_logits.float()).contiguous()
     tokens = draft_tokens.to(torch.int64).contiguous()
     temps = None
     if temperatures is not None:
@@ -73,12 +75,13 @@ def verify_batch(draft_probs: torch.Tensor, target_logits: torch.Tensor, draft_t
     L = _lib.lib()
     need = int(L.sdb_verify_workspace_size(B, k, Tr, V))
     ws = _lib.WORKSPACES.get(draft.device, "verify", need)
-    rc = L.sdb_verify_batch(draft.data_ptr(), target.data_ptr(), tokens.data_ptr(), _lib.ptr(temps),
-                            _lib.ptr(u), _lib.ptr(e), int(seed) & (2**64 - 1), int(offset) & (2**64 - 1),
-                            1 if draft_is_point_mass else 0, out.accepted.data_ptr(),
-                            out.bonus.data_ptr(), out.accept_mask.data_ptr(), B, k, Tr, V,
-                            ws.data_ptr(), ws.numel(), _lib.stream_of(draft))
-    _lib.check(rc, "sdb_verify_batch")
+    rc = L.sdb_verify_batch_ex(draft.data_ptr(), _lib.DTYPE_CODE[draft.dtype], target.data_ptr(),
+                               _lib.DTYPE_CODE[target.dtype], tokens.data_ptr(), _lib.ptr(temps),
+                               _lib.ptr(u), _lib.ptr(e), int(seed) & (2**64 - 1), int(offset) & (2**64 - 1),
+                               1 if draft_is_point_mass else 0, out.accepted.data_ptr(),
+                               out.bonus.data_ptr(), out.accept_mask.data_ptr(), B, k, Tr, V,
+                               ws.data_ptr(), ws.numel(), _lib.stream_of(draft))
+    _lib.check(rc, "sdb_verify_batch_ex")
     return out
 
 

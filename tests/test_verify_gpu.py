@@ -220,3 +220,43 @@ def test_graph_capture_with_fixed_draws(pkg):
     assert torch.equal(out.accepted, ref[0]) and torch.equal(out.bonus, ref[1])
     assert torch.equal(out.accept_mask, ref[2])
     del g
+
+
+# ------------------------------------------------------------ 16-bit logits (no float32 copy)
+@pytest.mark.parametrize("ddt,tdt", [(torch.float32, torch.bfloat16), (torch.bfloat16, torch.bfloat16),
+                                     (torch.float16, torch.float16), (torch.bfloat16, torch.float32)])
+@pytest.mark.parametrize("V", [151936, 997, 4100])
+def test_16bit_logits_equal_float32_path(pkg, ddt, tdt, V):
+    """The engine passes the LM head's bf16 logits (model_runner.py:1101-1103) and the
+    reference converts with .float(): decisions and tokens must equal the float32 path on
+    the converted values bit for bit (V 997: scalar rows; 4100: V % 8 != 0, no bulk copy
+    for 16-bit rows)."""
+    g = torch.Generator().manual_seed(V + 3)
+    B, k = 12, 5
+    target = (torch.randn(B, k + 1, V, generator=g) * 3.0).to(tdt).cuda()
+    draft = (target[:, :k].float() + torch.randn(B, k, V, generator=g).cuda()).to(ddt)
+    tokens = torch.randint(0, V, (B, k), generator=g).cuda()
+    temps = torch.linspace(0.6, 1.4, B).cuda()
+    temps[0] = 1.0
+    r16 = pkg.verify_batch(draft, target, tokens, temps, seed=77, offset=5)
+    r32 = pkg.verify_batch(draft.float(), target.float(), tokens, temps, seed=77, offset=5)
+    torch.cuda.synchronize()
+    assert torch.equal(r16.accepted, r32.accepted)
+    assert torch.equal(r16.accept_mask, r32.accept_mask)
+    assert torch.equal(r16.bonus, r32.bonus)
+
+
+def test_cfg4_bf16_target_full_size_against_oracle(pkg):
+    """cfg4 with the target logits in bf16 as the LM head emits them."""
+    from specdec_nanovllm_b200.workloads import cfg4_inputs
+    draft, target, tokens = cfg4_inputs(seed=1)
+    target = target.to(torch.bfloat16)
+    seed, off = 99, 3
+    r = pkg.verify_batch(draft, target, tokens, None, seed=seed, offset=off)
+    torch.cuda.synchronize()
+    want = ov.verify_batch(draft.cpu().numpy(), target.float().cpu().numpy(), tokens.cpu().numpy(), None,
+                           uniforms=philox.uniforms(seed, off, 64, 6),
+                           exponentials=philox.exponentials(seed, off, 64, 151936))
+    assert np.array_equal(r.accepted.cpu().numpy(), want.accepted)
+    assert np.array_equal(r.accept_mask.cpu().numpy(), want.accept_mask)
+    assert np.array_equal(r.bonus.cpu().numpy(), want.bonus)
