@@ -267,6 +267,36 @@ int sdb_verify_batch_ex(const void* draft_logits, int draft_dtype,
                         int B, int k, int target_rows, int V,
                         void* workspace, size_t workspace_bytes, void* stream);
 
+/* verify_batch over vocabulary shards: the LM head split by columns across tp ranks
+ * (ParallelLMHead, nanovllm/layers/embed_head.py:56-75).  The reference gathers the
+ * full logits on rank 0 (:71-74); here every rank keeps its shard and the ranks
+ * exchange per-sequence statistics only.  Four phases; between phases the caller
+ * all-gathers each rank's `send` buffer (sdb_verify_shard_send_floats(B, k,
+ * target_rows, phase) floats) into `gathered` in rank order (tp x that many):
+ *   1: local statistics; send = per sequence each row's (max, sum exp) and the
+ *      candidates' logits on the rank that owns their columns (NaN elsewhere)
+ *   2: the decisions from the gathered summaries (out_accepted, out_accept_mask),
+ *      then this rank's residual / p sums of row `accepted`; send = those sums
+ *   3: this rank's bonus argmax under the global normaliser; send = (best value,
+ *      global column as float bits)
+ *   4: out_bonus from the gathered bests
+ * Draws are keyed by global columns (the single-device streams).  Every rank ends
+ * with identical outputs, equal to sdb_verify_batch_ex on the full logits except
+ * where two values tie within float32 rounding (the shards' sums are added in another
+ * order).  vocab_start: this rank's first column; V_local its column count; the
+ * workspace (sdb_verify_workspace_size(B, k, target_rows, V_local)) carries the
+ * decisions from phase 2 to phases 3-4: keep it between the phases of one call. */
+size_t sdb_verify_shard_send_floats(int B, int k, int target_rows, int phase);
+int sdb_verify_batch_shard(int phase, const void* draft_logits, int draft_dtype,
+                           const void* target_logits, int target_dtype,
+                           const int64_t* draft_tokens, const float* temperatures,
+                           const float* uniforms, const float* exponentials,
+                           uint64_t seed, uint64_t offset, int draft_is_point_mass,
+                           int64_t* out_accepted, int64_t* out_bonus, uint8_t* out_accept_mask,
+                           int B, int k, int target_rows, int V_local, int vocab_start, int V_total,
+                           int tp, const float* gathered, float* send,
+                           void* workspace, size_t workspace_bytes, void* stream);
+
 /* Philox streams of the samplers written out (test and debugging aid): stream 0
  * as uniforms [rows, cols], stream 1 (verify_batch) or 2 (sample) as
  * exponentials [rows, cols]. */

@@ -8,7 +8,8 @@ CUDA kernels.  Public surface, mirroring the reference's call signatures:
 * ``attention``: ``Attention``, ``paged_attention``, ``paged_decode_attention``,
   ``paged_decode_attention_cuda``, ``flash_attn_with_kvcache``,
   ``flash_attn_varlen_func``, ``store_kvcache``
-* ``verify``: ``verify_batch`` -> ``VerifyResult``
+* ``verify``: ``verify_batch`` -> ``VerifyResult``; ``verify_batch_vocab_parallel`` over
+  vocabulary shards (three small all-gathers instead of gathering the logits)
 * ``sampler``: ``Sampler``, ``sample``, ``draft_sample_step``
 * ``prologue``: ``qk_norm_rope_store`` (split + q/k RMSNorm + rotary + KV store),
   ``rope_cos_sin_cache``
@@ -25,7 +26,7 @@ from .context import Context, get_context, reset_context, set_context  # noqa: F
 from .quant import dequantize_weight, int8_linear, quantize_weight  # noqa: F401
 from .prologue import qk_norm_rope_store, rope_cos_sin_cache  # noqa: F401
 from .sampler import Sampler, draft_sample_step, sample  # noqa: F401
-from .verify import VerifyResult, verify_batch  # noqa: F401
+from .verify import VerifyResult, VocabParallelVerify, verify_batch, verify_batch_vocab_parallel  # noqa: F401
 
 LIB_PATH = _lib.LIB_PATH
 

@@ -80,6 +80,10 @@ SIGNATURES = {
     "sdb_verify_batch_ex": (_c_i32, [
         _c_p, _c_i32, _c_p, _c_i32, _c_p, _c_p, _c_p, _c_p, _c_u64, _c_u64, _c_i32, _c_p, _c_p, _c_p,
         _c_i32, _c_i32, _c_i32, _c_i32, _c_p, _c_sz, _c_p]),
+    "sdb_verify_shard_send_floats": (_c_sz, [_c_i32] * 4),
+    "sdb_verify_batch_shard": (_c_i32, [
+        _c_i32, _c_p, _c_i32, _c_p, _c_i32, _c_p, _c_p, _c_p, _c_p, _c_u64, _c_u64, _c_i32, _c_p, _c_p, _c_p,
+        _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_p, _c_p, _c_p, _c_sz, _c_p]),
     "sdb_philox_fill": (_c_i32, [_c_p, _c_i32, _c_i32, _c_u64, _c_u64, _c_i32, _c_p]),
     "sdb_qk_norm_rope_store": (_c_i32, [
         _c_p, _c_i64, _c_p, _c_p, _c_f32, _c_p, _c_i64, _c_i32, _c_p,

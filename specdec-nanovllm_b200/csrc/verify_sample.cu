@@ -69,6 +69,13 @@ struct Params {
     int* counters;         // [B], zero between calls
     struct Decision* dec;  // [B]
     int* err;
+    // vocabulary-parallel form (the LM head split by columns across tp ranks): this
+    // rank holds global columns [col0, col0 + V) of Vg; `gathered` holds the previous
+    // exchange of all tp ranks (rank-major), `send` receives this rank's next one.
+    // Single-device calls: col0 = 0, Vg = V, shard = 0.
+    int col0, Vg, tp, shard;
+    const float* gathered;
+    float* send;
 };
 
 SDB_DEV float accept_uniform(const Params& p, int b, int j) {
@@ -372,59 +379,47 @@ __global__ void __launch_bounds__(BS_THREADS, 2) vs_row_stats_bulk(const Params 
 // ratio = where(q_tok > 0, min(p_tok / max(q_tok, 1e-10), 1), 0); accept = u < ratio
 // (verify.py:109-121); accepted = first rejection or k (:125-129).
 constexpr int DECIDE_THREADS = 512;
-__global__ void __launch_bounds__(DECIDE_THREADS) vs_decide(const Params p) {
-    __shared__ float sM[65], sI[65];
-    const int b = blockIdx.x;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nd = p.B * p.k;
-    const int nrows = p.k + p.Tr;
-    for (int r = warp; r < nrows; r += DECIDE_THREADS / 32) {
-        if (r < p.k && p.point_mass) continue;
-        const int grow = r < p.k ? b * p.k + r : nd + b * p.Tr + (r - p.k);
-        const float2* st = p.stats + (int64_t)grow * p.C1 * SUB;
-        const int np = p.C1 * SUB;
-        constexpr int kHeld = 16;  // partials per lane kept in registers (V up to 2^22)
-        float2 h[kHeld];
-        float M = -INFINITY;
+
+// (max, sum exp(x - max)) of global row `grow` from its chunk partials, on every lane
+// of the calling warp.
+SDB_DEV float2 merge_row_stats(const Params& p, int grow, int lane) {
+    const float2* st = p.stats + (int64_t)grow * p.C1 * SUB;
+    const int np = p.C1 * SUB;
+    constexpr int kHeld = 16;  // partials per lane kept in registers (V up to 2^22)
+    float2 h[kHeld];
+    float M = -INFINITY;
 #pragma unroll
-        for (int j = 0; j < kHeld; ++j) {
-            const int c = lane + 32 * j;
-            h[j] = c < np ? __ldcg(st + c) : make_float2(-INFINITY, 0.f);
-            M = fmaxf(M, h[j].x);
-        }
-        for (int c = lane + 32 * kHeld; c < np; c += 32) M = fmaxf(M, __ldcg(st + c).x);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-        float S = 0.f;
-#pragma unroll
-        for (int j = 0; j < kHeld; ++j)
-            if (h[j].x != -INFINITY) S += h[j].y * expf(h[j].x - M);
-        for (int c = lane + 32 * kHeld; c < np; c += 32) {
-            const float2 v = __ldcg(st + c);
-            if (v.x != -INFINITY) S += v.y * expf(v.x - M);
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) S += __shfl_xor_sync(0xffffffffu, S, o);
-        if (lane == 0) {
-            sM[r] = M;
-            sI[r] = 1.0f / S;
-        }
+    for (int j = 0; j < kHeld; ++j) {
+        const int c = lane + 32 * j;
+        h[j] = c < np ? __ldcg(st + c) : make_float2(-INFINITY, 0.f);
+        M = fmaxf(M, h[j].x);
     }
-    __syncthreads();
-    if (warp != 0) return;
+    for (int c = lane + 32 * kHeld; c < np; c += 32) M = fmaxf(M, __ldcg(st + c).x);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    float S = 0.f;
+#pragma unroll
+    for (int j = 0; j < kHeld; ++j)
+        if (h[j].x != -INFINITY) S += h[j].y * expf(h[j].x - M);
+    for (int c = lane + 32 * kHeld; c < np; c += 32) {
+        const float2 v = __ldcg(st + c);
+        if (v.x != -INFINITY) S += v.y * expf(v.x - M);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) S += __shfl_xor_sync(0xffffffffu, S, o);
+    return make_float2(M, S);
+}
+
+// Warp-wide: the k acceptance decisions of sequence b given every row's max sM and
+// inverse sum sI (draft rows 0..k-1, target rows k..k+Tr-1) and, on lane j < k, the
+// draft and target logits of candidate j (verify.py:109-129); writes the Decision and
+// the outputs.
+SDB_DEV void decide_from(const Params& p, int b, int lane, const float* sM, const float* sI, float xq, float xp) {
     const float T = p.temps ? p.temps[b] : 1.0f;
     bool acc = true;
     if (lane < p.k) {
-        int64_t tok = p.tokens[b * p.k + lane];
-        if (tok < 0 || tok >= p.V) {
-            atomicOr(p.err, SDB_KERR_TOKEN);
-            tok = 0;
-        }
-        const int drow = b * p.k + lane;
-        const float xq = draft_row(p, drow).at(tok);
         const float q_tok = p.point_mass ? xq : expf(scale_t(xq, T) - sM[lane]) * sI[lane];
-        const float p_tok =
-            expf(scale_t(target_row(p, b * p.Tr + lane).at(tok), T) - sM[p.k + lane]) * sI[p.k + lane];
+        const float p_tok = expf(scale_t(xp, T) - sM[p.k + lane]) * sI[p.k + lane];
         const float ratio = q_tok > 0.f ? fminf(__fdiv_rn(p_tok, fmaxf(q_tok, 1e-10f)), 1.0f) : 0.f;
         acc = accept_uniform(p, b, lane) < ratio;
         p.out_mask[b * p.k + lane] = acc ? 1 : 0;
@@ -446,6 +441,146 @@ __global__ void __launch_bounds__(DECIDE_THREADS) vs_decide(const Params p) {
         p.dec[b] = d;
         p.out_acc[b] = a;
     }
+}
+
+// Candidate j's token, range-checked against the (global) vocabulary.
+SDB_DEV int64_t candidate_token(const Params& p, int b, int j) {
+    int64_t tok = p.tokens[b * p.k + j];
+    if (tok < 0 || tok >= p.Vg) {
+        atomicOr(p.err, SDB_KERR_TOKEN);
+        tok = 0;
+    }
+    return tok;
+}
+
+__global__ void __launch_bounds__(DECIDE_THREADS) vs_decide(const Params p) {
+    __shared__ float sM[65], sI[65];
+    const int b = blockIdx.x;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nd = p.B * p.k;
+    const int nrows = p.k + p.Tr;
+    for (int r = warp; r < nrows; r += DECIDE_THREADS / 32) {
+        if (r < p.k && p.point_mass) continue;
+        const int grow = r < p.k ? b * p.k + r : nd + b * p.Tr + (r - p.k);
+        const float2 ms = merge_row_stats(p, grow, lane);
+        if (lane == 0) {
+            sM[r] = ms.x;
+            sI[r] = 1.0f / ms.y;
+        }
+    }
+    __syncthreads();
+    if (warp != 0) return;
+    float xq = 0.f, xp = 0.f;
+    if (lane < p.k) {
+        const int64_t tok = candidate_token(p, b, lane);
+        xq = draft_row(p, b * p.k + lane).at(tok);
+        xp = target_row(p, b * p.Tr + lane).at(tok);
+    }
+    decide_from(p, b, lane, sM, sI, xq, xp);
+}
+
+// ------------------------------------------------------------------ vocabulary-parallel form
+// Exchange 1 (this rank -> all): per sequence, every row's local (max, sum) and, for
+// each candidate, its draft and target logit if this rank owns the token's column
+// (NaN otherwise).  Layout per sequence: M[k+Tr], S[k+Tr], xq[k], xp[k].
+SDB_DEV int summary_floats(const Params& p) { return 2 * (p.k + p.Tr) + 2 * p.k; }
+
+__global__ void __launch_bounds__(DECIDE_THREADS) vs_summary(const Params p) {
+    const int b = blockIdx.x;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nd = p.B * p.k;
+    const int nrows = p.k + p.Tr;
+    float* out = p.send + (int64_t)b * summary_floats(p);
+    for (int r = warp; r < nrows; r += DECIDE_THREADS / 32) {
+        float2 ms = make_float2(-INFINITY, 0.f);
+        if (!(r < p.k && p.point_mass)) {
+            const int grow = r < p.k ? b * p.k + r : nd + b * p.Tr + (r - p.k);
+            ms = merge_row_stats(p, grow, lane);
+        }
+        if (lane == 0) {
+            out[r] = ms.x;
+            out[nrows + r] = ms.y;
+        }
+    }
+    if (warp == 0 && lane < p.k) {
+        const int64_t tok = candidate_token(p, b, lane);
+        const bool own = tok >= p.col0 && tok < (int64_t)p.col0 + p.V;
+        out[2 * nrows + lane] = own ? draft_row(p, b * p.k + lane).at(tok - p.col0) : __int_as_float(0x7fc00000);
+        out[2 * nrows + p.k + lane] = own ? target_row(p, b * p.Tr + lane).at(tok - p.col0) : __int_as_float(0x7fc00000);
+    }
+}
+
+// After exchange 1: every rank merges the tp summaries in rank order (so all ranks hold
+// identical statistics) and makes the same decisions.  One warp per sequence.
+__global__ void __launch_bounds__(32) vs_decide_shard(const Params p) {
+    __shared__ float sM[65], sI[65];
+    const int b = blockIdx.x, lane = threadIdx.x;
+    const int nrows = p.k + p.Tr, F = summary_floats(p);
+    for (int r = lane; r < nrows; r += 32) {
+        float M = -INFINITY;
+        for (int t = 0; t < p.tp; ++t) M = fmaxf(M, p.gathered[((int64_t)t * p.B + b) * F + r]);
+        float S = 0.f;
+        for (int t = 0; t < p.tp; ++t) {
+            const float* g = p.gathered + ((int64_t)t * p.B + b) * F;
+            if (g[r] != -INFINITY) S += g[nrows + r] * expf(g[r] - M);
+        }
+        sM[r] = M;
+        sI[r] = 1.0f / S;
+    }
+    __syncwarp();
+    float xq = 0.f, xp = 0.f;
+    if (lane < p.k) {
+        candidate_token(p, b, lane);  // the range check
+        for (int t = 0; t < p.tp; ++t) {  // exactly one rank owns the column
+            const float* g = p.gathered + ((int64_t)t * p.B + b) * F;
+            const float q = g[2 * nrows + lane], x = g[2 * nrows + p.k + lane];
+            if (!isnan(x)) {
+                xq = q;
+                xp = x;
+            }
+        }
+    }
+    decide_from(p, b, lane, sM, sI, xq, xp);
+}
+
+// Exchange 2: this rank's residual and p sums of row a (the chunk sums of pass 3).
+__global__ void __launch_bounds__(256) vs_rsum_total(const Params p) {
+    const int lane = threadIdx.x & 31;
+    const int b = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (b >= p.B) return;
+    float sr = 0.f, sp = 0.f;
+    for (int cc = lane; cc < p.C2; cc += 32) {
+        const float2 v = __ldcg(p.rsum + b * p.C2 + cc);
+        sr += v.x;
+        sp += v.y;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        sr += __shfl_xor_sync(0xffffffffu, sr, o);
+        sp += __shfl_xor_sync(0xffffffffu, sp, o);
+    }
+    if (lane == 0) {
+        p.send[2 * b] = sr;
+        p.send[2 * b + 1] = sp;
+    }
+}
+
+// After exchange 3 (each rank's (best value, global column) of the bonus argmax): the
+// first index among the largest values, ranks holding increasing column ranges.
+__global__ void vs_bonus_finish(const Params p) {
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= p.B) return;
+    float gb = -INFINITY;
+    int gi = 0x7fffffff;
+    for (int t = 0; t < p.tp; ++t) {
+        const float v = p.gathered[((int64_t)t * p.B + b) * 2];
+        const int i = __float_as_int(p.gathered[((int64_t)t * p.B + b) * 2 + 1]);
+        if (v > gb || (v == gb && i < gi)) {
+            gb = v;
+            gi = i;
+        }
+    }
+    p.out_bonus[b] = gi == 0x7fffffff ? 0 : gi;
 }
 
 // resid_i and p_i of row a (verify.py:141-148): q_pad[k] = 0, p index clamped.
@@ -542,12 +677,12 @@ __global__ void __launch_bounds__(THREADS) vs_resid_sums(const Params p) {
 
 SDB_DEV bool better(float v, int i, float bv, int bi) { return v > bv || (v == bv && i < bi); }
 
-// max(E, 1e-10) for columns i .. i + cnt - 1 of sequence b (cnt = 4: i % 4 == 0, one
-// Philox block gives the four words).
+// max(E, 1e-10) for global columns i .. i + cnt - 1 of sequence b (cnt = 4: i % 4 == 0,
+// one Philox block gives the four words).
 SDB_DEV void exp_noise4(const Params& p, int b, int i, int cnt, float (&E)[4]) {
     if (p.e) {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) E[e] = e < cnt ? p.e[(int64_t)b * p.V + i + e] : 1.f;
+        for (int e = 0; e < 4; ++e) E[e] = e < cnt ? p.e[(int64_t)b * p.Vg + i + e] : 1.f;
     } else if (cnt == 4) {
         uint32_t c[4] = {(uint32_t)i >> 2, (uint32_t)b, 1u, p.offset};
         philox(c, p.seed_lo, p.seed_hi);
@@ -568,12 +703,20 @@ __global__ void __launch_bounds__(THREADS) vs_bonus(const Params p) {
     __shared__ int bi[THREADS / 32];
     const int b = blockIdx.x, c = blockIdx.y;
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    if (threadIdx.x < 32) {  // the chunk sums of pass 3, loaded by all lanes at once
+    if (threadIdx.x < 32) {  // the chunk sums of pass 3 (every rank's totals in the
+                             // vocabulary-parallel form), loaded by all lanes at once
         float sr = 0.f, sp = 0.f;
-        for (int cc = lane; cc < p.C2; cc += 32) {
-            const float2 v = __ldcg(p.rsum + b * p.C2 + cc);
-            sr += v.x;
-            sp += v.y;
+        if (p.shard) {
+            for (int t = lane; t < p.tp; t += 32) {
+                sr += p.gathered[((int64_t)t * p.B + b) * 2];
+                sp += p.gathered[((int64_t)t * p.B + b) * 2 + 1];
+            }
+        } else {
+            for (int cc = lane; cc < p.C2; cc += 32) {
+                const float2 v = __ldcg(p.rsum + b * p.C2 + cc);
+                sr += v.x;
+                sp += v.y;
+            }
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
@@ -600,16 +743,16 @@ __global__ void __launch_bounds__(THREADS) vs_bonus(const Params p) {
         resid_of<decltype(unit)::value>(p, d, T, xt, xd, r, pv);
         const float v = up ? pv : r;
         const float x = v != 0.f ? __fdiv_rn(__fdiv_rn(v, Z), E) : 0.f;  // 0 / Z / E is +0
-        if (better(x, i, best, bidx)) {
+        if (better(x, p.col0 + i, best, bidx)) {  // global column
             best = x;
-            bidx = i;
+            bidx = p.col0 + i;
         }
     };
     auto body = [&](auto unit) {
         if (!p.vec) {
             for_chunk(p, tr, dr, c * CHUNK2, [&](int i, const float4& xt, const float4& xd) {
                 float E[4];
-                exp_noise4(p, b, i, 1, E);
+                exp_noise4(p, b, p.col0 + i, 1, E);
                 exact(unit, i, xt.x, xd.x, E[0]);
             });
             return;
@@ -648,14 +791,14 @@ __global__ void __launch_bounds__(THREADS) vs_bonus(const Params p) {
             const bool in = idx < n;
             const float t4[4] = {xt[q].x, xt[q].y, xt[q].z, xt[q].w};
             const float d4[4] = {xd[q].x, xd[q].y, xd[q].z, xd[q].w};
-            uint32_t w4[4] = {(uint32_t)(base + idx) >> 2, (uint32_t)b, 1u, p.offset};
+            uint32_t w4[4] = {(uint32_t)(p.col0 + base + idx) >> 2, (uint32_t)b, 1u, p.offset};
             if (!p.e && in) philox(w4, p.seed_lo, p.seed_hi);
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
                 const int j = 4 * q + e;
                 float Elo, Ehi;
                 if (p.e) {
-                    Elo = Ehi = in ? fmaxf(p.e[(int64_t)b * p.V + base + idx + e], 1e-10f) : 1.f;
+                    Elo = Ehi = in ? fmaxf(p.e[(int64_t)b * p.Vg + p.col0 + base + idx + e], 1e-10f) : 1.f;
                 } else {
                     // -log U in [1 - U, (1 - U)(3 - 2U)] for U >= 1/2 and <= 17 always
                     // (U >= 2^-24); 1 - U is exact (U is a multiple of 2^-24); the factors
@@ -692,9 +835,9 @@ __global__ void __launch_bounds__(THREADS) vs_bonus(const Params p) {
             const int j = __ffs(live) - 1;
             live &= live - 1;
             const int i = base + group_col(j >> 2) + (j & 3);
-            const float E = p.e ? fmaxf(p.e[(int64_t)b * p.V + i], 1e-10f)
+            const float E = p.e ? fmaxf(p.e[(int64_t)b * p.Vg + p.col0 + i], 1e-10f)
                                 : fmaxf(-log_fixed(word_to_open_uniform(philox_word(
-                                            p.seed_lo, p.seed_hi, p.offset, 1u, (uint32_t)b, (uint32_t)i))),
+                                            p.seed_lo, p.seed_hi, p.offset, 1u, (uint32_t)b, (uint32_t)(p.col0 + i)))),
                                         1e-10f);
             exact(unit, i, tr.at(i), dr.p ? dr.at(i) : 0.f, E);
         }
@@ -751,7 +894,12 @@ __global__ void __launch_bounds__(THREADS) vs_bonus(const Params p) {
         }
     }
     if (lane == 0) {
-        p.out_bonus[b] = gi == 0x7fffffff ? 0 : gi;
+        if (p.shard) {  // exchange 3: this rank's best value and its global column
+            p.send[2 * b] = gb;
+            p.send[2 * b + 1] = __int_as_float(gi);
+        } else {
+            p.out_bonus[b] = gi == 0x7fffffff ? 0 : gi;
+        }
         p.counters[b] = 0;
     }
 }
@@ -803,18 +951,24 @@ extern "C" size_t sdb_verify_workspace_size(int B, int k, int target_rows, int V
     return vs::ws_layout(B, k, target_rows, V).total;
 }
 
-extern "C" int sdb_verify_batch_ex(const void* draft, int draft_dtype, const void* target, int target_dtype,
-                                   const int64_t* tokens, const float* temps, const float* uniforms,
-                                   const float* exponentials, uint64_t seed, uint64_t offset, int point_mass,
-                                   int64_t* out_acc, int64_t* out_bonus, uint8_t* out_mask, int B, int k, int Tr,
-                                   int V, void* workspace, size_t workspace_bytes, void* stream) {
+namespace {
+
+// Validation and parameter block shared by the single-device and the
+// vocabulary-parallel entry points.  V is this rank's column count, [col0, col0 + V)
+// its columns of the Vg-wide vocabulary.
+int setup(vs::Params& p, const void* draft, int draft_dtype, const void* target, int target_dtype,
+          const int64_t* tokens, const float* temps, const float* uniforms, const float* exponentials, uint64_t seed,
+          uint64_t offset, int point_mass, int64_t* out_acc, int64_t* out_bonus, uint8_t* out_mask, int B, int k,
+          int Tr, int V, int col0, int Vg, void* workspace, size_t workspace_bytes) {
     if (!draft || !target || !tokens || !out_acc || !out_bonus || !out_mask || !workspace) {
         set_last_error("null pointer argument");
         return SDB_ERR_INVALID_ARG;
     }
-    if (B <= 0 || B > vs::kCounterCap || k <= 0 || k > 32 || V <= 0 || !(Tr == k || Tr == k + 1)) {
-        set_last_error("bad sizes B=%d k=%d target_rows=%d V=%d (need B <= %d, 1<=k<=32, target_rows in {k, k+1})",
-                       B, k, Tr, V, vs::kCounterCap);
+    if (B <= 0 || B > vs::kCounterCap || k <= 0 || k > 32 || V <= 0 || !(Tr == k || Tr == k + 1) || col0 < 0 ||
+        (long long)col0 + V > Vg) {
+        set_last_error("bad sizes B=%d k=%d target_rows=%d V=%d columns [%d, %lld) of %d (need B <= %d, "
+                       "1<=k<=32, target_rows in {k, k+1})",
+                       B, k, Tr, V, col0, (long long)col0 + V, Vg, vs::kCounterCap);
         return SDB_ERR_INVALID_ARG;
     }
     auto kind_of = [](int dt) { return dt == SDB_F32 ? 0 : (dt == SDB_BF16 ? 1 : (dt == SDB_F16 ? 2 : -1)); };
@@ -834,7 +988,7 @@ extern "C" int sdb_verify_batch_ex(const void* draft, int draft_dtype, const voi
         return SDB_ERR_WORKSPACE;
     }
     uint8_t* ws = reinterpret_cast<uint8_t*>(workspace);
-    vs::Params p{};
+    p = vs::Params{};
     p.draft = draft;
     p.target = target;
     p.dkind = dkind;
@@ -854,6 +1008,9 @@ extern "C" int sdb_verify_batch_ex(const void* draft, int draft_dtype, const voi
     p.k = k;
     p.Tr = Tr;
     p.V = V;
+    p.col0 = col0;
+    p.Vg = Vg;
+    p.tp = 1;
     p.C1 = (V + vs::CHUNK1 - 1) / vs::CHUNK1;
     p.C2 = (V + vs::CHUNK2 - 1) / vs::CHUNK2;
     p.err = reinterpret_cast<int*>(ws + w.err);
@@ -862,29 +1019,47 @@ extern "C" int sdb_verify_batch_ex(const void* draft, int draft_dtype, const voi
     p.stats = reinterpret_cast<float2*>(ws + w.stats);
     p.rsum = reinterpret_cast<float2*>(ws + w.rsum);
     p.amax = reinterpret_cast<float2*>(ws + w.amax);
-    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    const int row0 = point_mass ? B * k : 0;
-    const int nrows = B * ((point_mass ? 0 : k) + Tr);
-    // bulk copies need every streamed row to be a whole number of 16-byte units (the
-    // bases were checked above): V % 4 == 0 for float32 rows, V % 8 == 0 for 16-bit ones
     // passes 3-4 read 16-byte vectors when every row they read is 16-byte aligned (the
-    // point-mass draft is read too: its residual row)
-    p.vec = (V & 3) == 0 && (dkind == 0 || (V & 7) == 0) && (tkind == 0 || (V & 7) == 0);
-    const bool draft_rows_ok = point_mass || ((V * (dkind == 0 ? 4 : 2)) % 16 == 0);
-    const bool target_rows_ok = (V * (tkind == 0 ? 4 : 2)) % 16 == 0;
-    int rc;
-    if ((V & 3) == 0 && draft_rows_ok && target_rows_ok) {
-        rc = ensure_smem_attr(reinterpret_cast<const void*>(vs::vs_row_stats_bulk), vs::BS_SMEM, 50);
+    // point-mass draft is read too: its residual row) and Philox groups of four columns
+    // start on this rank's group boundaries
+    p.vec = (V & 3) == 0 && (col0 & 3) == 0 && (dkind == 0 || (V & 7) == 0) && (tkind == 0 || (V & 7) == 0);
+    return SDB_OK;
+}
+
+// Pass 1 over this rank's rows.
+int launch_stats(const vs::Params& p, cudaStream_t st) {
+    const int row0 = p.point_mass ? p.B * p.k : 0;
+    const int nrows = p.B * ((p.point_mass ? 0 : p.k) + p.Tr);
+    // bulk copies need every streamed row to be a whole number of 16-byte units (the
+    // bases were checked): V % 4 == 0 for float32 rows, V % 8 == 0 for 16-bit ones
+    const bool draft_rows_ok = p.point_mass || ((p.V * (p.dkind == 0 ? 4 : 2)) % 16 == 0);
+    const bool target_rows_ok = (p.V * (p.tkind == 0 ? 4 : 2)) % 16 == 0;
+    if ((p.V & 3) == 0 && draft_rows_ok && target_rows_ok) {
+        int rc = ensure_smem_attr(reinterpret_cast<const void*>(vs::vs_row_stats_bulk), vs::BS_SMEM, 50);
         if (rc) return rc;
         const long long items = (long long)nrows * p.C1;
         const int slots = 2 * device_sm_count();
         const int grid = (int)(items < slots ? items : slots);
         vs::vs_row_stats_bulk<<<grid, vs::BS_THREADS, vs::BS_SMEM, st>>>(p, row0, nrows);
-        rc = cuda_status(cudaGetLastError(), "vs_row_stats_bulk launch");
-    } else {
-        vs::vs_row_stats<<<dim3(nrows, p.C1), vs::THREADS, 0, st>>>(p);
-        rc = cuda_status(cudaGetLastError(), "vs_row_stats launch");
+        return cuda_status(cudaGetLastError(), "vs_row_stats_bulk launch");
     }
+    vs::vs_row_stats<<<dim3(nrows, p.C1), vs::THREADS, 0, st>>>(p);
+    return cuda_status(cudaGetLastError(), "vs_row_stats launch");
+}
+
+}  // namespace
+
+extern "C" int sdb_verify_batch_ex(const void* draft, int draft_dtype, const void* target, int target_dtype,
+                                   const int64_t* tokens, const float* temps, const float* uniforms,
+                                   const float* exponentials, uint64_t seed, uint64_t offset, int point_mass,
+                                   int64_t* out_acc, int64_t* out_bonus, uint8_t* out_mask, int B, int k, int Tr,
+                                   int V, void* workspace, size_t workspace_bytes, void* stream) {
+    vs::Params p;
+    int rc = setup(p, draft, draft_dtype, target, target_dtype, tokens, temps, uniforms, exponentials, seed, offset,
+                   point_mass, out_acc, out_bonus, out_mask, B, k, Tr, V, 0, V, workspace, workspace_bytes);
+    if (rc) return rc;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    rc = launch_stats(p, st);
     if (rc) return rc;
     vs::vs_decide<<<B, vs::DECIDE_THREADS, 0, st>>>(p);
     rc = cuda_status(cudaGetLastError(), "vs_decide launch");
@@ -894,6 +1069,58 @@ extern "C" int sdb_verify_batch_ex(const void* draft, int draft_dtype, const voi
     if (rc) return rc;
     vs::vs_bonus<<<dim3(B, p.C2), vs::THREADS, 0, st>>>(p);
     return cuda_status(cudaGetLastError(), "vs_bonus launch");
+}
+
+extern "C" size_t sdb_verify_shard_send_floats(int B, int k, int target_rows, int phase) {
+    if (B <= 0 || k <= 0 || target_rows <= 0) return 0;
+    if (phase == 1) return (size_t)B * (2 * (k + target_rows) + 2 * k);
+    if (phase == 2 || phase == 3) return (size_t)B * 2;
+    return 0;
+}
+
+extern "C" int sdb_verify_batch_shard(int phase, const void* draft, int draft_dtype, const void* target,
+                                      int target_dtype, const int64_t* tokens, const float* temps,
+                                      const float* uniforms, const float* exponentials, uint64_t seed,
+                                      uint64_t offset, int point_mass, int64_t* out_acc, int64_t* out_bonus,
+                                      uint8_t* out_mask, int B, int k, int Tr, int V_local, int vocab_start,
+                                      int V_total, int tp, const float* gathered, float* send, void* workspace,
+                                      size_t workspace_bytes, void* stream) {
+    if (phase < 1 || phase > 4 || tp < 1 || (phase > 1 && !gathered) || (phase < 4 && !send)) {
+        set_last_error("bad phase %d / tp %d / exchange buffers for sdb_verify_batch_shard", phase, tp);
+        return SDB_ERR_INVALID_ARG;
+    }
+    vs::Params p;
+    int rc = setup(p, draft, draft_dtype, target, target_dtype, tokens, temps, uniforms, exponentials, seed, offset,
+                   point_mass, out_acc, out_bonus, out_mask, B, k, Tr, V_local, vocab_start, V_total, workspace,
+                   workspace_bytes);
+    if (rc) return rc;
+    p.tp = tp;
+    p.shard = 1;
+    p.gathered = gathered;
+    p.send = send;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    switch (phase) {
+        case 1:  // local statistics -> exchange 1
+            rc = launch_stats(p, st);
+            if (rc) return rc;
+            vs::vs_summary<<<B, vs::DECIDE_THREADS, 0, st>>>(p);
+            return cuda_status(cudaGetLastError(), "vs_summary launch");
+        case 2:  // decisions from exchange 1, local residual sums -> exchange 2
+            vs::vs_decide_shard<<<B, 32, 0, st>>>(p);
+            rc = cuda_status(cudaGetLastError(), "vs_decide_shard launch");
+            if (rc) return rc;
+            vs::vs_resid_sums<<<dim3(B, p.C2), vs::THREADS, 0, st>>>(p);
+            rc = cuda_status(cudaGetLastError(), "vs_resid_sums launch");
+            if (rc) return rc;
+            vs::vs_rsum_total<<<(B + 7) / 8, 256, 0, st>>>(p);
+            return cuda_status(cudaGetLastError(), "vs_rsum_total launch");
+        case 3:  // local bonus argmax with the global normaliser of exchange 2 -> exchange 3
+            vs::vs_bonus<<<dim3(B, p.C2), vs::THREADS, 0, st>>>(p);
+            return cuda_status(cudaGetLastError(), "vs_bonus launch");
+        default:  // the bonus token from exchange 3
+            vs::vs_bonus_finish<<<(B + 127) / 128, 128, 0, st>>>(p);
+            return cuda_status(cudaGetLastError(), "vs_bonus_finish launch");
+    }
 }
 
 extern "C" int sdb_verify_batch(const float* draft, const float* target, const int64_t* tokens, const float* temps,

@@ -260,3 +260,62 @@ def test_cfg4_bf16_target_full_size_against_oracle(pkg):
     assert np.array_equal(r.accepted.cpu().numpy(), want.accepted)
     assert np.array_equal(r.accept_mask.cpu().numpy(), want.accept_mask)
     assert np.array_equal(r.bonus.cpu().numpy(), want.bonus)
+
+
+# ------------------------------------------------------------ vocabulary-parallel form
+def _shards(V, tp):
+    base, extra = divmod(V, tp)
+    out, s = [], 0
+    for r in range(tp):
+        n = base + (1 if r < extra else 0)
+        out.append((s, s + n))
+        s += n
+    return out
+
+
+def _run_vp_emulated(pkg, draft, target, tokens, temps, point, tp, **kw):
+    """All tp ranks' phases on one GPU, the all-gathers emulated by concatenation."""
+    V = draft.shape[2]
+    ranks = [pkg.VocabParallelVerify(draft[:, :, s:e], target[:, :, s:e], tokens, temps, point,
+                                     vocab_start=s, vocab_size=V, tp=tp, **kw) for s, e in _shards(V, tp)]
+    gathered = None
+    for n in (1, 2, 3, 4):
+        sends = [r.phase(n, gathered) for r in ranks]
+        gathered = torch.cat(sends) if sends[0] is not None else None
+    return [r.result for r in ranks]
+
+
+@pytest.mark.parametrize("tp", [2, 3, 8])
+@pytest.mark.parametrize("V,tdt,point", [(151936, torch.float32, False), (151936, torch.bfloat16, False),
+                                         (997, torch.float32, False), (4100, torch.float32, True)])
+def test_vocab_parallel_equals_single_device(pkg, tp, V, tdt, point):
+    g = torch.Generator().manual_seed(V * 7 + tp)
+    B, k = 16, 6
+    target = (torch.randn(B, k + 1, V, generator=g) * 3.0).to(tdt).cuda()
+    tokens = torch.randint(0, V, (B, k), generator=g).cuda()
+    if point:
+        draft = torch.zeros(B, k, V).scatter_(2, tokens.cpu().unsqueeze(-1), 1.0).cuda()
+    else:
+        draft = target[:, :k].float() + torch.randn(B, k, V, generator=g).cuda()
+    temps = torch.linspace(0.7, 1.3, B).cuda()
+    temps[3] = 1.0
+    want = pkg.verify_batch(draft, target, tokens, temps, point, seed=5, offset=9)
+    results = _run_vp_emulated(pkg, draft, target, tokens, temps, point, tp, seed=5, offset=9)
+    torch.cuda.synchronize()
+    for r in results:  # every rank holds the same result, equal to the single-device call
+        assert torch.equal(r.accepted, want.accepted)
+        assert torch.equal(r.accept_mask, want.accept_mask)
+        assert torch.equal(r.bonus, want.bonus)
+    assert 0 < int(want.accepted.sum()) < B * k or point
+
+
+def test_vocab_parallel_injected_draws_match_oracle(pkg, golden):
+    g = golden("verify_temps")
+    B, k, V = g["draft"].shape
+    res = _run_vp_emulated(pkg, _t(g["draft"]), _t(g["target"]), _t(g["tokens"]), _t(g["temps"]), False, 3,
+                           seed=0, offset=0, uniforms=_t(g["u"]), exponentials=_t(g["e"]))
+    torch.cuda.synchronize()
+    for r in res:
+        assert np.array_equal(r.accepted.cpu().numpy(), g["accepted"])
+        assert np.array_equal(r.accept_mask.cpu().numpy(), g["accept_mask"])
+        assert np.array_equal(r.bonus.cpu().numpy(), g["bonus"])
