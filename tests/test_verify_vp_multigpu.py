@@ -1,7 +1,7 @@
-"""verify_batch over vocabulary shards on 2 GPUs (one process per GPU, NCCL).
-
-Every rank must return the single-device result on the full logits.  Skipped when
-fewer than two GPUs are visible.
+"""The multi-GPU forms on 2 GPUs (one process per GPU, NCCL): verify_batch over
+vocabulary shards (every rank must return the single-device result on the full
+logits) and the row-parallel W8A16 projection (all-reduced partial sums against the
+single-device product, bf16 bar).  Skipped when fewer than two GPUs are visible.
 """
 
 import os
@@ -47,6 +47,25 @@ def _worker(rank, world, port, results):
         torch.cuda.synchronize()
         results[rank] = (torch.equal(r.accepted, want.accepted), torch.equal(r.accept_mask, want.accept_mask),
                          torch.equal(r.bonus, want.bonus), int(want.accepted.sum()))
+        # row-parallel o_proj (linear.py:165-170): each rank multiplies its input slice
+        from specdec_nanovllm_b200.partition import RowParallelInt8Linear
+        from specdec_nanovllm_b200.workloads import cfg3_inputs
+        x, q, sc = cfg3_inputs(64, 4096, 2560, seed=4)
+        layer = RowParallelInt8Linear(q, sc, None, rank, world)
+        ks = 4096 // world
+        y = layer(x[:, rank * ks:(rank + 1) * ks].contiguous())
+        # the same partial products made on one device and added in fp16, as NCCL adds them
+        parts = [pkg.int8_linear(x[:, r * ks:(r + 1) * ks].contiguous(), q[:, r * ks:(r + 1) * ks].contiguous(), sc)
+                 for r in range(world)]
+        emulated = parts[0]
+        for pr in parts[1:]:
+            emulated = emulated + pr
+        full = pkg.int8_linear(x, q, sc)
+        torch.cuda.synchronize()
+        # against the one-device product: the fp16 rounding of each partial (|partial| up to
+        # ~200, half an ulp 0.06) on top of the bf16 bar
+        bound = 2e-2 * full.float().abs() + 2e-3 + sum(pr.float().abs() for pr in parts) * 2.0 ** -11
+        results[f"tp{rank}"] = (torch.equal(y, emulated), float(((y.float() - full.float()).abs() - bound).max()))
         dist.barrier()
     finally:
         dist.destroy_process_group()
@@ -63,3 +82,5 @@ def test_two_gpus_nccl():
         acc, mask, bonus, n = res[rank]
         assert acc and mask and bonus, res
         assert 0 < n < 32 * 6
+        same, excess = res[f"tp{rank}"]
+        assert same and excess <= 0.0, res
