@@ -13,12 +13,14 @@
 // columns [0, 64), O^T head / residual parts in [64, 96) / [96, 128).  K, V and Q
 // arrive by TMA in the 128-byte-swizzled layout the MMA descriptors read directly
 // (K as a K-major A operand, V as an MN-major A operand, Q^T as a K-major B
-// operand); P is written by the softmax warps key-major (an MN-major B operand).
+// operand); P is written by the softmax warps key-major into its own buffer (an
+// MN-major B operand).
 // P is split into a 16-bit head and a 16-bit residual and both multiply V, so the
 // probabilities keep ~16 significant bits.
 //
 // Warp roles (320 threads, one CTA per SM, persistent over work items):
-//   warp 0      TMA producer: Q of each item, K/V tiles of 128 keys into a 3-stage ring
+//   warp 0      TMA producer: Q of each item, K and V tiles of 128 keys into two
+//               3-slot rings (a K slot is released by S(t), a V slot by P.V(t))
 //   warp 1      TMEM owner and MMA issuer (one thread)
 //   warps 2..9  (fused store_kvcache only) first copy the step's new K/V rows of
 //               the CTA's items into the cache, then
@@ -43,27 +45,35 @@ namespace umma {
 
 constexpr int UBN = 128;                  // keys per tile
 constexpr int UHALF = UBN * 128;          // one 64-dim half of a K or V tile: 16 KB
-constexpr int UTILE = 2 * UHALF;          // 32 KB
-constexpr int USTAGE = 2 * UTILE;         // K + V: 64 KB
-constexpr int UNS = 3;                    // stages
+constexpr int UTILE = 2 * UHALF;          // one K or V tile: 32 KB
+// K and V tiles stream through two rings of UNS slots each.  A K slot is released
+// when S(t) has read it and a V slot when P.V(t) has, so each ring holds a tile from
+// its load until its own last use: tile t + UNS can be loaded UNS tile-intervals
+// before it is needed (a shared K+V stage, released only after P.V, gave K two).
+constexpr int UNS = 3;                    // slots per ring
 constexpr int NROW = 32;                  // MMA N: query rows per (sequence, kv head)
 constexpr int QHALF = NROW * 128;         // 4 KB
-// P of tile t is written into the first K half of tile t's stage once S(t) has read
-// K, as one N = 64 B operand: 128 key rows of 128 B, columns 0..31 the 16-bit heads
-// of the 32 rows' probabilities, columns 32..63 their residuals, so a single MMA per
-// key step reads V once and accumulates O_head and O_residual side by side (64 TMEM
-// columns).  The stage ring thus multi-buffers P and the P.V completion that frees
-// the stage also frees P.
+// P of tile t is written into its own buffer, as one N = 64 B operand: 128 key rows
+// of 128 B, columns 0..31 the 16-bit heads of the 32 rows' probabilities, columns
+// 32..63 their residuals, so a single MMA per key step reads V once and accumulates
+// O_head and O_residual side by side (64 TMEM columns).  The completion of P.V(t)
+// frees the buffer (p_free) before the softmax writes P(t + 1).
 constexpr int PROWS = 2 * NROW;
+constexpr int PBYTES = UBN * 128;         // 16 KB
 constexpr int QBUF = 2 * QHALF;           // one item's Q^T (8 KB)
-constexpr int OFF_Q = UNS * USTAGE;       // two Q^T buffers: item i uses buffer i & 1
+constexpr int OFF_K = 0;                  // K ring
+constexpr int OFF_V = UNS * UTILE;        // V ring
+constexpr int OFF_P = 2 * UNS * UTILE;    // P
+constexpr int OFF_Q = OFF_P + PBYTES;     // two Q^T buffers: item i uses buffer i & 1
 constexpr int OFF_RED = OFF_Q + 2 * QBUF;             // red_max[4][32], red_sum[4][32]
 constexpr int kMaxUmmaSplits = 16;
 constexpr int OFF_BAR = OFF_RED + 2 * 4 * 32 * 4;
-// barriers: full[3] empty[3] s_full[2] s_free[2] p_full q_ready[2] q_free[2] fin stored
-constexpr int NBAR = UNS * 2 + 2 + 2 + 1 + 2 + 2 + 1 + 1;
+// barriers: k_full[3] k_empty[3] v_full[3] v_empty[3] s_full[2] s_free[2] p_full
+// p_free q_ready[2] q_free[2] fin stored
+constexpr int NBAR = UNS * 4 + 2 + 2 + 1 + 1 + 2 + 2 + 1 + 1;
 constexpr int OFF_TMEM = OFF_BAR + NBAR * 8;
 constexpr int SMEM_BYTES = OFF_TMEM + 16 + 1024;  // + alignment slack
+static_assert(SMEM_BYTES <= 232448, "exceeds the 227 KB of shared memory a CTA may use");
 // TMEM columns: S^T buffers [0, 64), O^T heads / residuals [64, 96) / [96, 128)
 constexpr uint32_t TMEM_COLS = 128;
 constexpr uint32_t TCOL_O = 64;
@@ -72,17 +82,20 @@ constexpr int SOFTMAX_WARPS = SOFTMAX_THREADS / 32;  // one mbarrier arrival per
 constexpr int THREADS = 64 + SOFTMAX_THREADS;
 
 struct Bars {
-    uint32_t full0, empty0, sfull0, sfree0, pfull, qready0, qfree0, fin, stored;
+    uint32_t kfull0, kempty0, vfull0, vempty0, sfull0, sfree0, pfull, pfree, qready0, qfree0, fin, stored;
 };
 
 SDB_DEV Bars bars_at(uint32_t base) {
     Bars b;
-    b.full0 = base;
-    b.empty0 = base + 8 * UNS;
-    b.sfull0 = base + 16 * UNS;
+    b.kfull0 = base;
+    b.kempty0 = base + 8 * UNS;
+    b.vfull0 = base + 16 * UNS;
+    b.vempty0 = base + 24 * UNS;
+    b.sfull0 = base + 32 * UNS;
     b.sfree0 = b.sfull0 + 16;
     b.pfull = b.sfree0 + 16;
-    b.qready0 = b.pfull + 8;
+    b.pfree = b.pfull + 8;
+    b.qready0 = b.pfree + 8;
     b.qfree0 = b.qready0 + 16;
     b.fin = b.qfree0 + 16;
     b.stored = b.fin + 8;
@@ -322,14 +335,17 @@ __global__ void __launch_bounds__(THREADS, 1)
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < UNS; ++s) {
-            mbar_init(bar.full0 + 8 * s, 1);
-            mbar_init(bar.empty0 + 8 * s, 1);
+            mbar_init(bar.kfull0 + 8 * s, 1);
+            mbar_init(bar.kempty0 + 8 * s, 1);
+            mbar_init(bar.vfull0 + 8 * s, 1);
+            mbar_init(bar.vempty0 + 8 * s, 1);
         }
         for (int i = 0; i < 2; ++i) {
             mbar_init(bar.sfull0 + 8 * i, 1);
             mbar_init(bar.sfree0 + 8 * i, SOFTMAX_WARPS);
         }
         mbar_init(bar.pfull, SOFTMAX_WARPS);
+        mbar_init(bar.pfree, 1);
         for (int i = 0; i < 2; ++i) {
             mbar_init(bar.qready0 + 8 * i, 1);
             mbar_init(bar.qfree0 + 8 * i, 1);
@@ -359,7 +375,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             prefetch_tensormap(&qmap);
             const uint64_t pol = l2_policy_evict_first();
             const uint64_t qpol = l2_policy_evict_normal();  // every split of a sequence reads Q
-            int gt = 0, nq = 0;
+            int gt = 0, nq = 0, kextra = 0;
             bool ok = true;
             bool stored = p.slots == nullptr;  // no fused store: nothing to wait for
             int need_tile = INT_MAX;
@@ -387,7 +403,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                     ++nq;
                 }
                 const int s = gt % UNS;
-                if (gt >= UNS && !mbar_wait(bar.empty0 + 8 * s, ((gt / UNS) - 1) & 1)) {
+                // slot s of the K ring is free once S(gt - UNS) has completed
+                if (gt >= UNS && !mbar_wait(bar.kempty0 + 8 * s, ((gt / UNS) - 1) & 1)) {
                     ok = false;
                     break;
                 }
@@ -404,20 +421,34 @@ __global__ void __launch_bounds__(THREADS, 1)
                     blk = 0;
                 }
                 const int off = j % p.page;
-                const uint32_t kdst = sbase + s * USTAGE;
-                const uint32_t vdst = kdst + UTILE;
-                const uint32_t fb = bar.full0 + 8 * s;
-                mbar_arrive_expect_tx(fb, USTAGE);
-                tma_load_4d(kdst, &kmap, fb, 0, ld.x.kvh, off, blk, pol);
-                tma_load_4d(kdst + UHALF, &kmap, fb, 64, ld.x.kvh, off, blk, pol);
-                tma_load_4d(vdst, &vmap, fb, 0, ld.x.kvh, off, blk, pol);
-                tma_load_4d(vdst + UHALF, &vmap, fb, 64, ld.x.kvh, off, blk, pol);
+                const uint32_t kdst = sbase + OFF_K + s * UTILE;
+                const uint32_t vdst = sbase + OFF_V + s * UTILE;
+                const uint32_t kb = bar.kfull0 + 8 * s, vb = bar.vfull0 + 8 * s;
+                mbar_arrive_expect_tx(kb, UTILE);
+                tma_load_4d(kdst, &kmap, kb, 0, ld.x.kvh, off, blk, pol);
+                tma_load_4d(kdst + UHALF, &kmap, kb, 64, ld.x.kvh, off, blk, pol);
+                // slot s of the V ring is free once P.V(gt - UNS) has completed
+                if (gt >= UNS && !mbar_wait(bar.vempty0 + 8 * s, ((gt / UNS) - 1) & 1)) {
+                    ok = false;
+                    kextra = 1;  // this tile's K copy is in flight: drained below
+                    break;
+                }
+                mbar_arrive_expect_tx(vb, UTILE);
+                tma_load_4d(vdst, &vmap, vb, 0, ld.x.kvh, off, blk, pol);
+                tma_load_4d(vdst + UHALF, &vmap, vb, 64, ld.x.kvh, off, blk, pol);
                 ++gt;
                 ld.advance(p);
             }
             if (!ok) atomicOr(p.err, SDB_KERR_TIMEOUT);
-            for (int g = gt - UNS > 0 ? gt - UNS : 0; g < gt; ++g) {  // drain own copies
-                if (!mbar_wait(bar.full0 + 8 * (g % UNS), (g / UNS) & 1)) {
+            // drain own copies: K of tiles < gt + kextra, V of tiles < gt
+            for (int g = gt + kextra - UNS > 0 ? gt + kextra - UNS : 0; g < gt + kextra; ++g) {
+                if (!mbar_wait(bar.kfull0 + 8 * (g % UNS), (g / UNS) & 1)) {
+                    atomicOr(p.err, SDB_KERR_TIMEOUT);
+                    break;
+                }
+            }
+            for (int g = gt - UNS > 0 ? gt - UNS : 0; g < gt; ++g) {
+                if (!mbar_wait(bar.vfull0 + 8 * (g % UNS), (g / UNS) & 1)) {
                     atomicOr(p.err, SDB_KERR_TIMEOUT);
                     break;
                 }
@@ -438,18 +469,21 @@ __global__ void __launch_bounds__(THREADS, 1)
             int gt = 0, nitem = 0;
             bool ok = true;
             // O^T += V(g)^T . P(g), heads and residuals as N = 64; completion frees stage g (K, V and P)
+            // O^T += V(g)^T . P(g); completion frees V slot g % UNS and the P buffer
             auto pv = [&](int g, bool first, uint32_t ocol) -> bool {
-                if (!mbar_wait(bar.pfull, g & 1)) return false;
+                if (!mbar_wait(bar.pfull, g & 1) || !mbar_wait(bar.vfull0 + 8 * (g % UNS), (g / UNS) & 1))
+                    return false;
                 tc_fence_after();
-                const uint32_t stage = sbase + (g % UNS) * USTAGE;
-                const uint32_t vbase = stage + UTILE;
+                const uint32_t vbase = sbase + OFF_V + (g % UNS) * UTILE;
+                const uint32_t pbase = sbase + OFF_P;
 #pragma unroll
                 for (int ks = 0; ks < 8; ++ks) {
                     const uint64_t a = sdesc_sw128(vbase + ks * 2048, UHALF, 1024);
-                    const uint64_t b = sdesc_sw128(stage + ks * 2048, UHALF, 1024);
+                    const uint64_t b = sdesc_sw128(pbase + ks * 2048, UHALF, 1024);
                     umma_f16_ss(tmem + ocol, a, b, IDESC_PV, (first && ks == 0) ? 0u : 1u);
                 }
-                umma_commit(bar.empty0 + 8 * (g % UNS));
+                umma_commit(bar.vempty0 + 8 * (g % UNS));
+                umma_commit(bar.pfree);
                 return true;
             };
             // nitem counts the items that have tiles: only those take a Q buffer / q_ready phase
@@ -465,13 +499,13 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const uint32_t ocol = TCOL_O;
                 for (int t = 0; t < x.ntiles; ++t, ++gt) {
                     const int s = gt % UNS, sb = gt & 1;
-                    if (!mbar_wait(bar.full0 + 8 * s, (gt / UNS) & 1) ||
+                    if (!mbar_wait(bar.kfull0 + 8 * s, (gt / UNS) & 1) ||
                         (gt >= 2 && !mbar_wait(bar.sfree0 + 8 * sb, ((gt >> 1) - 1) & 1))) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t kbase = sbase + s * USTAGE;
+                    const uint32_t kbase = sbase + OFF_K + s * UTILE;
 #pragma unroll
                     for (int ks = 0; ks < 8; ++ks) {
                         const uint64_t a = sdesc_sw128(kbase + (ks >> 2) * UHALF + (ks & 3) * 32, 16, 1024);
@@ -480,6 +514,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                         umma_f16_ss(tmem + sb * 32, a, b, IDESC_S, ks > 0 ? 1u : 0u);
                     }
                     umma_commit(bar.sfull0 + 8 * sb);
+                    umma_commit(bar.kempty0 + 8 * s);  // K slot read
                     if (t == x.ntiles - 1) umma_commit(bar.qfree0 + 8 * (nitem & 1));  // Q buffer read
                     if (t >= 1 && !pv(gt - 1, t == 1, ocol)) {
                         ok = false;
@@ -630,9 +665,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                         lpart[i] *= av[i];
                     }
                     if (t >= 1) {
-                        // P.V(t-1) complete (it frees stage t-1): O is up to date, rescale it
-                        const int g1 = gt - 1;
-                        wait_or_skip(bar.empty0 + 8 * (g1 % UNS), (g1 / UNS) & 1, ok);
+                        // P.V(t-1) complete (p_free): O is up to date, rescale it
+                        wait_or_skip(bar.pfree, (gt - 1) & 1, ok);
                         tc_fence_after();
                         uint32_t oh[16], ol[16];
                         tmem_ld16(tmem + lane_addr + ocol + c0, oh);
@@ -656,24 +690,27 @@ __global__ void __launch_bounds__(THREADS, 1)
                 }
                 // keys past the split end: zero their V rows (unwritten cache may hold NaN)
                 const int kin = 32 * qt + lane;
-                uint8_t* stage = smem + s * USTAGE;
                 if (j0 + UBN > x.k1) {
-                    wait_or_skip(bar.full0 + 8 * s, (gt / UNS) & 1, ok);
+                    wait_or_skip(bar.vfull0 + 8 * s, (gt / UNS) & 1, ok);
                     if (j0 + kin >= x.k1) {
-                        uint8_t* vrow = stage + UTILE + kin * 128 + ch * UHALF;
+                        uint8_t* vrow = smem + OFF_V + s * UTILE + kin * 128 + ch * UHALF;
 #pragma unroll
                         for (int q16 = 0; q16 < 8; ++q16)
                             *reinterpret_cast<uint4*>(vrow + q16 * 16) = make_uint4(0, 0, 0, 0);
                     }
                 }
-                // P into the first K half of this stage (S(t) has read K): row `key` holds
-                // 64 columns, heads of rows 0..31 then their residuals, 128-byte swizzle
+                // P into the P buffer once P.V(t-1) has read it: row `key` holds 64
+                // columns, heads of rows 0..31 then their residuals, 128-byte swizzle
                 // (16-byte chunk j of row k at j ^ (k & 7)): the MN-major B operand of P.V
                 {
                     uint32_t hw[8], lw[8];
 #pragma unroll
                     for (int i = 0; i < 8; ++i) H::split2(pv[2 * i], pv[2 * i + 1], hw[i], lw[i]);
-                    uint8_t* prow = stage + kin * 128;
+                    if (gt >= 1) {
+                        wait_or_skip(bar.pfree, (gt - 1) & 1, ok);
+                        tc_fence_after();
+                    }
+                    uint8_t* prow = smem + OFF_P + kin * 128;
                     const int sw = kin & 7;
                     *reinterpret_cast<uint4*>(prow + (((2 * ch) ^ sw) << 4)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
                     *reinterpret_cast<uint4*>(prow + (((2 * ch + 1) ^ sw) << 4)) = make_uint4(hw[4], hw[5], hw[6], hw[7]);
@@ -698,9 +735,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const int cc = c0 + lc;
                 lsum = (red_sum[cc] + red_sum[32 + cc]) + (red_sum[64 + cc] + red_sum[96 + cc]);
             }
-            // the last P.V (it frees the last stage) has completed: O^T is final
-            const int g1 = gt - 1;
-            wait_or_skip(bar.empty0 + 8 * (g1 % UNS), (g1 / UNS) & 1, ok);
+            // the last P.V has completed (p_free): O^T is final
+            wait_or_skip(bar.pfree, (gt - 1) & 1, ok);
             tc_fence_after();
             {
                 uint32_t oh[16], ol[16];
