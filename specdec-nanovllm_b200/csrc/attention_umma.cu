@@ -19,8 +19,9 @@
 // probabilities keep ~16 significant bits.
 //
 // Warp roles (320 threads, one CTA per SM, persistent over work items):
-//   warp 0      TMA producer: Q of each item, K and V tiles of 128 keys into two
-//               3-slot rings (a K slot is released by S(t), a V slot by P.V(t))
+//   warp 0      TMA producers: lane 0 Q of each item and K tiles of 128 keys, lane 1
+//               V tiles, into two 3-slot rings (a K slot is released by S(t), a V slot
+//               by P.V(t))
 //   warp 1      TMEM owner and MMA issuer (one thread)
 //   warps 2..9  (fused store_kvcache only) first copy the step's new K/V rows of
 //               the CTA's items into the cache, then
@@ -368,43 +369,58 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t tmem = *tmem_slot;
 
     if (warp == 0) {
-        // ------------------------------------------------------------- producer
-        if (lane == 0) {
-            prefetch_tensormap(&kmap);
-            prefetch_tensormap(&vmap);
-            prefetch_tensormap(&qmap);
+        // ------------------------------------------------------------- producers
+        // lane 0 loads Q and the K ring, lane 1 the V ring: each ring refills a slot as
+        // soon as its own last reader (S for K, P.V for V) has completed, independently
+        // of the other ring's waits
+        if (lane < 2) {
+            const bool isk = lane == 0;
+            if (isk) {
+                prefetch_tensormap(&kmap);
+                prefetch_tensormap(&qmap);
+            } else {
+                prefetch_tensormap(&vmap);
+            }
+            const CUtensorMap* map = isk ? &kmap : &vmap;
+            const uint32_t full0 = isk ? bar.kfull0 : bar.vfull0;
+            const uint32_t empty0 = isk ? bar.kempty0 : bar.vempty0;
+            const uint32_t ring = sbase + (isk ? OFF_K : OFF_V);
             const uint64_t pol = l2_policy_evict_first();
             const uint64_t qpol = l2_policy_evict_normal();  // every split of a sequence reads Q
-            int gt = 0, nq = 0, kextra = 0;
+            int gt = 0, nq = 0;
             bool ok = true;
             bool stored = p.slots == nullptr;  // no fused store: nothing to wait for
             int need_tile = INT_MAX;
             TileCursor ld(p);
             while (ld.valid()) {
                 const int j = ld.x.k0 + ld.t * UBN;
-                // the block id is read before the waits, off the stage-hold path
+                // the block id is read before the waits, off the slot-hold path
                 int blk = p.bt[(int64_t)ld.x.b * p.bt_stride + j / p.page];
                 if (ld.t == 0) {
                     if (!stored) {
                         const NewRows nr = new_rows(p, ld.x);
                         need_tile = nr.i0 < nr.i1 ? nr.tile : INT_MAX;
                     }
-                    // Q^T rows (r, g) -> row r*G + g of Q buffer nq & 1, K-major 128-byte swizzle;
-                    // the buffer is free once the S MMAs of the item two before have completed
-                    const int qb = nq & 1;
-                    if (nq >= 2 && !mbar_wait(bar.qfree0 + 8 * qb, ((nq >> 1) - 1) & 1)) {
-                        ok = false;
-                        break;
+                    if (isk) {
+                        // Q^T rows (r, g) -> row r*G + g of Q buffer nq & 1, K-major 128-byte
+                        // swizzle; the buffer is free once the S MMAs of the item two before
+                        // have completed
+                        const int qb = nq & 1;
+                        if (nq >= 2 && !mbar_wait(bar.qfree0 + 8 * qb, ((nq >> 1) - 1) & 1)) {
+                            ok = false;
+                            break;
+                        }
+                        const uint32_t qdst = sbase + OFF_Q + qb * QBUF;
+                        mbar_arrive_expect_tx(bar.qready0 + 8 * qb, 2 * 128 * p.R);
+                        tma_load_4d(qdst, &qmap, bar.qready0 + 8 * qb, 0, 0, ld.x.kvh, ld.x.b * p.n_q, qpol);
+                        tma_load_4d(qdst + QHALF, &qmap, bar.qready0 + 8 * qb, 64, 0, ld.x.kvh, ld.x.b * p.n_q,
+                                    qpol);
+                        ++nq;
                     }
-                    const uint32_t qdst = sbase + OFF_Q + qb * QBUF;
-                    mbar_arrive_expect_tx(bar.qready0 + 8 * qb, 2 * 128 * p.R);
-                    tma_load_4d(qdst, &qmap, bar.qready0 + 8 * qb, 0, 0, ld.x.kvh, ld.x.b * p.n_q, qpol);
-                    tma_load_4d(qdst + QHALF, &qmap, bar.qready0 + 8 * qb, 64, 0, ld.x.kvh, ld.x.b * p.n_q, qpol);
-                    ++nq;
                 }
                 const int s = gt % UNS;
-                // slot s of the K ring is free once S(gt - UNS) has completed
-                if (gt >= UNS && !mbar_wait(bar.kempty0 + 8 * s, ((gt / UNS) - 1) & 1)) {
+                // slot s is free once the last reader of tile gt - UNS has completed
+                if (gt >= UNS && !mbar_wait(empty0 + 8 * s, ((gt / UNS) - 1) & 1)) {
                     ok = false;
                     break;
                 }
@@ -417,38 +433,21 @@ __global__ void __launch_bounds__(THREADS, 1)
                     stored = true;
                 }
                 if (blk < 0 || blk >= p.num_blocks) {
-                    atomicOr(p.err, SDB_KERR_BLOCK_ID);
+                    if (isk) atomicOr(p.err, SDB_KERR_BLOCK_ID);
                     blk = 0;
                 }
                 const int off = j % p.page;
-                const uint32_t kdst = sbase + OFF_K + s * UTILE;
-                const uint32_t vdst = sbase + OFF_V + s * UTILE;
-                const uint32_t kb = bar.kfull0 + 8 * s, vb = bar.vfull0 + 8 * s;
-                mbar_arrive_expect_tx(kb, UTILE);
-                tma_load_4d(kdst, &kmap, kb, 0, ld.x.kvh, off, blk, pol);
-                tma_load_4d(kdst + UHALF, &kmap, kb, 64, ld.x.kvh, off, blk, pol);
-                // slot s of the V ring is free once P.V(gt - UNS) has completed
-                if (gt >= UNS && !mbar_wait(bar.vempty0 + 8 * s, ((gt / UNS) - 1) & 1)) {
-                    ok = false;
-                    kextra = 1;  // this tile's K copy is in flight: drained below
-                    break;
-                }
-                mbar_arrive_expect_tx(vb, UTILE);
-                tma_load_4d(vdst, &vmap, vb, 0, ld.x.kvh, off, blk, pol);
-                tma_load_4d(vdst + UHALF, &vmap, vb, 64, ld.x.kvh, off, blk, pol);
+                const uint32_t dst = ring + s * UTILE;
+                const uint32_t fb = full0 + 8 * s;
+                mbar_arrive_expect_tx(fb, UTILE);
+                tma_load_4d(dst, map, fb, 0, ld.x.kvh, off, blk, pol);
+                tma_load_4d(dst + UHALF, map, fb, 64, ld.x.kvh, off, blk, pol);
                 ++gt;
                 ld.advance(p);
             }
             if (!ok) atomicOr(p.err, SDB_KERR_TIMEOUT);
-            // drain own copies: K of tiles < gt + kextra, V of tiles < gt
-            for (int g = gt + kextra - UNS > 0 ? gt + kextra - UNS : 0; g < gt + kextra; ++g) {
-                if (!mbar_wait(bar.kfull0 + 8 * (g % UNS), (g / UNS) & 1)) {
-                    atomicOr(p.err, SDB_KERR_TIMEOUT);
-                    break;
-                }
-            }
-            for (int g = gt - UNS > 0 ? gt - UNS : 0; g < gt; ++g) {
-                if (!mbar_wait(bar.vfull0 + 8 * (g % UNS), (g / UNS) & 1)) {
+            for (int g = gt - UNS > 0 ? gt - UNS : 0; g < gt; ++g) {  // drain own copies
+                if (!mbar_wait(full0 + 8 * (g % UNS), (g / UNS) & 1)) {
                     atomicOr(p.err, SDB_KERR_TIMEOUT);
                     break;
                 }
