@@ -80,6 +80,7 @@ constexpr uint32_t TMEM_COLS = 128;
 constexpr uint32_t TCOL_O = 64;
 constexpr int SOFTMAX_THREADS = 256;  // 8 warps
 constexpr int SOFTMAX_WARPS = SOFTMAX_THREADS / 32;  // one mbarrier arrival per warp
+constexpr int GROUP_THREADS = SOFTMAX_THREADS / 2;   // the 4 softmax warps of a column half
 constexpr int THREADS = 64 + SOFTMAX_THREADS;
 
 struct Bars {
@@ -537,7 +538,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         // point mbv[i] of each of its 16 rows; if no logit of the tile exceeds its row's
         // reference by more than 8 (log2 units, p <= 256), one vote barrier confirms it,
         // P = 2^(x - ref) is written and the row sums accumulate per thread.  Otherwise
-        // (first tile of an item, or a row max that grew) all warps take the exact path:
+        // (first tile of an item, or a row max that grew) the 4 warps of the column half
+        // take the exact path:
         // column max over the 128 keys, new reference = max, partial sums and O rescaled.
         const int sw = warp - 2;            // 0..7
         if (p.slots != nullptr) {  // fused store_kvcache, before the first S tile arrives
@@ -547,6 +549,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int qt = warp & 3;
         const int ch = sw >> 2;
         const int c0 = 16 * ch;             // first column (row) of this thread
+        // the 4 warps of a column half exchange maxima and sums only among themselves:
+        // each half synchronises on its own named barrier (ids 1 and 2)
+        const int gbar = 1 + ch;
         const int lc = lane & 15;           // column whose reference this lane owns: c0 + lc
         const uint32_t lane_addr = (uint32_t)(32 * qt) << 16;
         const int R = p.R;
@@ -642,14 +647,14 @@ __global__ void __launch_bounds__(THREADS, 1)
                 bool need = false;
 #pragma unroll
                 for (int i = 0; i < 16; ++i) need |= xv[i] > mbv[i] + 8.0f;
-                if (barrier_or(1, SOFTMAX_THREADS, need)) {
-                    // exact path (uniform over the 8 warps)
+                if (barrier_or(gbar, GROUP_THREADS, need)) {
+                    // exact path (uniform over the 4 warps of this column half)
                     float tmp[16];
 #pragma unroll
                     for (int i = 0; i < 16; ++i) tmp[i] = xv[i];
                     const float wm = transpose_reduce16<true>(tmp, lane);
                     if (lane < 16) red_max[qt * 32 + c0 + lane] = wm;
-                    named_barrier_sync(1, SOFTMAX_THREADS);
+                    named_barrier_sync(gbar, GROUP_THREADS);
                     const int cc = c0 + lc;
                     const float M =
                         fmaxf(fmaxf(red_max[cc], red_max[32 + cc]), fmaxf(red_max[64 + cc], red_max[96 + cc]));
@@ -728,9 +733,9 @@ __global__ void __launch_bounds__(THREADS, 1)
             {
                 const float ws = transpose_reduce16<false>(lpart, lane);
                 // every warp has read the previous item's red_sum
-                named_barrier_sync(1, SOFTMAX_THREADS);
+                named_barrier_sync(gbar, GROUP_THREADS);
                 if (lane < 16) red_sum[qt * 32 + c0 + lane] = ws;
-                named_barrier_sync(1, SOFTMAX_THREADS);
+                named_barrier_sync(gbar, GROUP_THREADS);
                 const int cc = c0 + lc;
                 lsum = (red_sum[cc] + red_sum[32 + cc]) + (red_sum[64 + cc] + red_sum[96 + cc]);
             }
