@@ -18,11 +18,13 @@
 // P is split into a 16-bit head and a 16-bit residual and both multiply V, so the
 // probabilities keep ~16 significant bits.
 //
-// Warp roles (320 threads, one CTA per SM, persistent over work items):
+// Warp roles (352 threads, one CTA per SM, persistent over work items):
 //   warp 0      TMA producers: lane 0 Q of each item and K tiles of 128 keys, lane 1
 //               V tiles, into two 3-slot rings (a K slot is released by S(t), a V slot
 //               by P.V(t))
-//   warp 1      TMEM owner and MMA issuer (one thread)
+//   warp 1      TMEM owner and S issuer (one thread)
+//   warp 10     P.V issuer (one thread): S and P.V are issued independently, so the
+//               tensor core gets S(t+1) while P.V(t) still waits for the softmax
 //   warps 2..9  (fused store_kvcache only) first copy the step's new K/V rows of
 //               the CTA's items into the cache, then
 //               softmax: thread = one TMEM lane (a key of S^T, a dim of O^T) and
@@ -81,7 +83,8 @@ constexpr uint32_t TCOL_O = 64;
 constexpr int SOFTMAX_THREADS = 256;  // 8 warps
 constexpr int SOFTMAX_WARPS = SOFTMAX_THREADS / 32;  // one mbarrier arrival per warp
 constexpr int GROUP_THREADS = SOFTMAX_THREADS / 2;   // the 4 softmax warps of a column half
-constexpr int THREADS = 64 + SOFTMAX_THREADS;
+constexpr int PV_WARP = 2 + SOFTMAX_WARPS;  // the P.V issuer, after the softmax warps
+constexpr int THREADS = 64 + SOFTMAX_THREADS + 32;
 
 struct Bars {
     uint32_t kfull0, kempty0, vfull0, vempty0, sfull0, sfree0, pfull, pfree, qready0, qfree0, fin, stored;
@@ -352,7 +355,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             mbar_init(bar.qready0 + 8 * i, 1);
             mbar_init(bar.qfree0 + 8 * i, 1);
         }
-        mbar_init(bar.fin, 1);
+        mbar_init(bar.fin, 2);  // one commit from each MMA issuer
         mbar_init(bar.stored, SOFTMAX_WARPS);
         fence_mbarrier_init();
     }
@@ -461,31 +464,14 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
         }
     } else if (warp == 1) {
-        // ------------------------------------------------------------- MMA issuer
+        // ------------------------------------------------------------- S issuer
+        // S^T(t) = K(t) . Q^T, one thread; P.V has its own issuer (warp PV_WARP), so an
+        // S is never queued behind a P.V that waits for the softmax
         if (lane == 0) {
             constexpr bool BF = std::is_same<T, __nv_bfloat16>::value;
             constexpr uint32_t IDESC_S = idesc_f16(BF, false, false, 128, NROW);
-            constexpr uint32_t IDESC_PV = idesc_f16(BF, true, true, 128, PROWS);
             int gt = 0, nitem = 0;
             bool ok = true;
-            // O^T += V(g)^T . P(g), heads and residuals as N = 64; completion frees stage g (K, V and P)
-            // O^T += V(g)^T . P(g); completion frees V slot g % UNS and the P buffer
-            auto pv = [&](int g, bool first, uint32_t ocol) -> bool {
-                if (!mbar_wait(bar.pfull, g & 1) || !mbar_wait(bar.vfull0 + 8 * (g % UNS), (g / UNS) & 1))
-                    return false;
-                tc_fence_after();
-                const uint32_t vbase = sbase + OFF_V + (g % UNS) * UTILE;
-                const uint32_t pbase = sbase + OFF_P;
-#pragma unroll
-                for (int ks = 0; ks < 8; ++ks) {
-                    const uint64_t a = sdesc_sw128(vbase + ks * 2048, UHALF, 1024);
-                    const uint64_t b = sdesc_sw128(pbase + ks * 2048, UHALF, 1024);
-                    umma_f16_ss(tmem + ocol, a, b, IDESC_PV, (first && ks == 0) ? 0u : 1u);
-                }
-                umma_commit(bar.vempty0 + 8 * (g % UNS));
-                umma_commit(bar.pfree);
-                return true;
-            };
             // nitem counts the items that have tiles: only those take a Q buffer / q_ready phase
             for (WorkIter w(p); w.valid() && ok;) {
                 const Item x = w.item(p);
@@ -496,7 +482,6 @@ __global__ void __launch_bounds__(THREADS, 1)
                     break;
                 }
                 tc_fence_after();
-                const uint32_t ocol = TCOL_O;
                 for (int t = 0; t < x.ntiles; ++t, ++gt) {
                     const int s = gt % UNS, sb = gt & 1;
                     if (!mbar_wait(bar.kfull0 + 8 * s, (gt / UNS) & 1) ||
@@ -516,16 +501,46 @@ __global__ void __launch_bounds__(THREADS, 1)
                     umma_commit(bar.sfull0 + 8 * sb);
                     umma_commit(bar.kempty0 + 8 * s);  // K slot read
                     if (t == x.ntiles - 1) umma_commit(bar.qfree0 + 8 * (nitem & 1));  // Q buffer read
-                    if (t >= 1 && !pv(gt - 1, t == 1, ocol)) {
-                        ok = false;
-                        break;
-                    }
                 }
-                if (ok && !pv(gt - 1, x.ntiles == 1, ocol)) ok = false;
                 ++nitem;
             }
             if (!ok) atomicOr(p.err, SDB_KERR_TIMEOUT);
-            // every MMA this thread issued has completed before TMEM is released
+            // every MMA this thread issued has completed before TMEM is released (fin
+            // completes once both issuers have committed)
+            umma_commit(bar.fin);
+            if (!mbar_wait(bar.fin, 0)) atomicOr(p.err, SDB_KERR_TIMEOUT);
+        }
+    } else if (warp == PV_WARP) {
+        // ------------------------------------------------------------- P.V issuer
+        // O^T += V(g)^T . P(g), heads and residuals as N = 64; completion frees V slot
+        // g % UNS and the P buffer
+        if (lane == 0) {
+            constexpr bool BF = std::is_same<T, __nv_bfloat16>::value;
+            constexpr uint32_t IDESC_PV = idesc_f16(BF, true, true, 128, PROWS);
+            int gt = 0;
+            bool ok = true;
+            for (WorkIter w(p); w.valid() && ok;) {
+                const Item x = w.item(p);
+                w.next(p, x);
+                for (int t = 0; t < x.ntiles; ++t, ++gt) {
+                    if (!mbar_wait(bar.pfull, gt & 1) || !mbar_wait(bar.vfull0 + 8 * (gt % UNS), (gt / UNS) & 1)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t vbase = sbase + OFF_V + (gt % UNS) * UTILE;
+                    const uint32_t pbase = sbase + OFF_P;
+#pragma unroll
+                    for (int ks = 0; ks < 8; ++ks) {
+                        const uint64_t a = sdesc_sw128(vbase + ks * 2048, UHALF, 1024);
+                        const uint64_t b = sdesc_sw128(pbase + ks * 2048, UHALF, 1024);
+                        umma_f16_ss(tmem + TCOL_O, a, b, IDESC_PV, (t == 0 && ks == 0) ? 0u : 1u);
+                    }
+                    umma_commit(bar.vempty0 + 8 * (gt % UNS));
+                    umma_commit(bar.pfree);
+                }
+            }
+            if (!ok) atomicOr(p.err, SDB_KERR_TIMEOUT);
             umma_commit(bar.fin);
             if (!mbar_wait(bar.fin, 0)) atomicOr(p.err, SDB_KERR_TIMEOUT);
         }
