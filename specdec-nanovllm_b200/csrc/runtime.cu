@@ -100,6 +100,7 @@ int encode_tensor_map(CUtensorMap* map, CUtensorMapDataType dtype, cuuint32_t ra
 extern "C" const char* sdb_last_error(void) { return sdb::g_last_error; }
 
 extern "C" const char* sdb_build_info(void) {
-    return "specdec_b200 sm_100a: paged_attention(tcgen05+TMA, mma16816+TMA, simt-f32), "
-           "paged_attention_readonly, verify_batch(philox4x32-10), w8a16_linear, quantize_weight";
+    return "specdec_b200 sm_100a: paged_attention(tcgen05+TMA, mma16816+TMA, simt-f32; fused store_kvcache), "
+           "paged_attention_readonly, verify_batch(philox4x32-10; f32/bf16/f16 logits; vocab-parallel), "
+           "sample(gumbel-max), qk_norm_rope_store, w8a16_linear(tcgen05, mma16816), quantize_weight";
 }
