@@ -889,7 +889,7 @@ struct UmmaPlan {
     int splits;  // partial slots per pair (grouped) or the strided split count
 };
 static UmmaPlan umma_plan(int B, int Hkv, int page, int max_blocks, int sms) {
-    constexpr double kItemCost = 1.0, kMergeBase = 1.5, kMergePerSlot = 0.25, kGroupedTax = 1.08;
+    constexpr double kItemCost = 1.5, kMergeBase = 1.5, kMergePerSlot = 0.25, kGroupedTax = 1.08;
     const FlatShape fs = flat_shape(B, Hkv, page, max_blocks, sms);
     const long long pairs = (long long)B * Hkv;
     UmmaPlan best{false, 1};
