@@ -133,3 +133,69 @@ class RowParallelInt8Linear(torch.nn.Module):
         if self.tp_size > 1:
             dist.all_reduce(y, group=self.group)
         return y
+
+
+# ------------------------------------------------------- vocabulary-parallel embedding
+def vocab_shard(num_embeddings: int, tp: int, rank: int) -> tuple[int, int]:
+    """Rows [start, end) of the embedding / LM-head table held by ``rank``
+    (``VocabParallelEmbedding.__init__``, embed_head.py:19-23: equal shards, no remainder)."""
+    if num_embeddings % tp:
+        raise ValueError(f"vocabulary {num_embeddings} must divide by tp={tp}")
+    per = num_embeddings // tp
+    return rank * per, (rank + 1) * per
+
+
+class VocabParallelEmbedding(torch.nn.Module):
+    """Token embedding with the table split by rows across tp ranks
+    (``VocabParallelEmbedding``, embed_head.py:9-43).
+
+    Each rank looks up the ids that fall in its shard, zeroes the rows of the others
+    (:36-40) and the ranks sum their outputs with one all-reduce (:41).  ``weight`` is
+    the full table or this rank's shard (``weight_loader``, :27-32, narrows dim 0).
+    """
+
+    def __init__(self, weight: torch.Tensor, tp_rank: int = 0, tp_size: int = 1, group=None,
+                 num_embeddings: Optional[int] = None):
+        super().__init__()
+        n = num_embeddings if num_embeddings is not None else weight.shape[0]
+        self.vocab_start, self.vocab_end = vocab_shard(n, tp_size, tp_rank)
+        per = self.vocab_end - self.vocab_start
+        if weight.shape[0] == n and tp_size > 1:
+            weight = weight[self.vocab_start:self.vocab_end]
+        if weight.shape[0] != per:
+            raise ValueError(f"weight has {weight.shape[0]} rows, shard wants {per}")
+        self.weight = weight.contiguous()
+        self.num_embeddings = n
+        self.tp_rank, self.tp_size, self.group = tp_rank, tp_size, group
+
+    def forward(self, ids: torch.Tensor) -> torch.Tensor:
+        if self.tp_size == 1:
+            return torch.nn.functional.embedding(ids, self.weight)
+        mask = (ids >= self.vocab_start) & (ids < self.vocab_end)
+        y = torch.nn.functional.embedding(mask * (ids - self.vocab_start), self.weight)
+        y = mask.unsqueeze(-1) * y
+        dist.all_reduce(y, group=self.group)
+        return y
+
+
+class ParallelLMHead(VocabParallelEmbedding):
+    """LM head over the same row split (``ParallelLMHead``, embed_head.py:44-75).
+
+    ``forward(x)`` keeps the reference's contract: every rank computes its logit
+    columns and rank 0 gathers them into the full (tokens, V) row (:70-74; the other
+    ranks get None).  ``forward_shard(x)`` returns this rank's columns only, the
+    input of ``VocabParallelVerify`` / ``verify_batch_vocab_parallel``, which decide
+    the verify step from the shards and never assemble the 151936-wide row.
+    Trimming to the last row of each sequence at prefill (:66-68) is the caller's.
+    """
+
+    def forward_shard(self, x: torch.Tensor) -> torch.Tensor:
+        return torch.nn.functional.linear(x, self.weight)
+
+    def forward(self, x: torch.Tensor) -> Optional[torch.Tensor]:
+        logits = self.forward_shard(x)
+        if self.tp_size == 1:
+            return logits
+        parts = [torch.empty_like(logits) for _ in range(self.tp_size)] if self.tp_rank == 0 else None
+        dist.gather(logits, parts, dst=0, group=self.group)
+        return torch.cat(parts, dim=-1) if self.tp_rank == 0 else None

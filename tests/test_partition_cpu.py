@@ -52,7 +52,8 @@ def _worker(rank, world, port, results):
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
     try:
         load_package()
-        from specdec_nanovllm_b200.partition import (RowParallelInt8Linear, gather_step_results,
+        from specdec_nanovllm_b200.partition import (ParallelLMHead, RowParallelInt8Linear,
+                                                     VocabParallelEmbedding, gather_step_results,
                                                      sequence_shard)
         # --- sequence sharding: each rank produces results for its own sequences
         B = 7
@@ -78,6 +79,21 @@ def _worker(rank, world, port, results):
         y = layer(x[:, rank * ks:(rank + 1) * ks])
         full = ref_matmul(x, q, s, bias)
         results[f"tp{rank}"] = float((y - full).abs().max())
+        # --- vocabulary-parallel embedding and LM head (embed_head.py:33-75)
+        V, H = 10, 6
+        table = torch.randn(V, H, generator=g)
+        ids = torch.tensor([[0, 4, 5, 9], [7, 2, 3, 1]])
+        emb = VocabParallelEmbedding(table, rank, world)
+        results[f"emb{rank}"] = bool(torch.equal(emb(ids), table[ids]))
+        head = ParallelLMHead(table, rank, world)
+        h = torch.randn(3, H, generator=g)
+        full_logits = h @ table.T
+        shard = head.forward_shard(h)
+        lo, hi = rank * V // world, (rank + 1) * V // world
+        results[f"head_shard{rank}"] = bool(torch.allclose(shard, full_logits[:, lo:hi], atol=1e-6))
+        gathered = head(h)
+        results[f"head{rank}"] = (None if gathered is None
+                                  else bool(torch.allclose(gathered, full_logits, atol=1e-6)))
     finally:
         dist.destroy_process_group()
 
@@ -94,3 +110,18 @@ def test_gloo_two_ranks_sequence_gather_and_row_parallel_allreduce():
         assert acc == [i * 10 for i in range(7)]
         assert bonus == [i + 1000 for i in range(7)]
         assert res[f"tp{r}"] < 1e-4
+        assert res[f"emb{r}"] and res[f"head_shard{r}"]
+    assert res["head0"] is True and res["head1"] is None
+
+
+def test_vocab_shard_and_single_rank_embedding():
+    load_package()
+    from specdec_nanovllm_b200.partition import ParallelLMHead, VocabParallelEmbedding, vocab_shard
+    assert [vocab_shard(151936, 8, r) for r in (0, 7)] == [(0, 18992), (132944, 151936)]
+    with pytest.raises(ValueError):
+        vocab_shard(10, 3, 0)
+    t = torch.randn(12, 4)
+    ids = torch.tensor([3, 11, 0])
+    assert torch.equal(VocabParallelEmbedding(t)(ids), t[ids])
+    x = torch.randn(2, 4)
+    assert torch.allclose(ParallelLMHead(t)(x), x @ t.T)
