@@ -148,6 +148,34 @@ SDB_DEV void prefetch_tensormap(const CUtensorMap* map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
+// ---------------------------------------------------------------- clusters and PDL
+SDB_DEV uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+SDB_DEV uint32_t cluster_id_x() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+    return r;
+}
+// Every thread of every CTA in the cluster arrives (release) and waits (acquire): shared
+// memory written before it is visible to the cluster's other CTAs after it.
+SDB_DEV void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+// Generic address of the same shared-memory location in the CTA of rank `rank` of this
+// cluster; plain loads through it read that CTA's shared memory (DSMEM).
+SDB_DEV const void* dsmem_map(const void* p, uint32_t rank) {
+    uint64_t r;
+    asm("mapa.u64 %0, %1, %2;" : "=l"(r) : "l"(reinterpret_cast<uint64_t>(p)), "r"(rank));
+    return reinterpret_cast<const void*>(r);
+}
+// Programmatic dependent launch: let the next kernel in the stream start launching, and
+// wait until the preceding kernel has completed with its memory visible.
+SDB_DEV void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
+SDB_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 SDB_DEV void named_barrier_sync(int id, int nthreads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }

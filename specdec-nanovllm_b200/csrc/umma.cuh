@@ -45,6 +45,18 @@ SDB_DEV void umma_f16_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint
         : "memory");
 }
 
+// D[tmem] (+)= A[tmem] x B[smem desc], kind::f16.  A (M = 128 rows, K-major) sits in TMEM
+// lanes 0..127, two 16-bit k values per 32-bit column (lower k in the low half), so one
+// K = 16 step reads 8 columns from `a_tmem`.
+SDB_DEV void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+        ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+        : "memory");
+}
+
 // Arrive once on the mbarrier when every tcgen05 op issued so far by this thread completes.
 SDB_DEV void umma_commit(uint32_t mbar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(mbar)

@@ -285,6 +285,9 @@ size_t w8a16_umma_partial_bytes(int M, int N, int K);
 int w8a16_umma_launch(const void* x, int64_t x_srow, const int8_t* w, const void* s, int s_dtype, const void* bias,
                       void* y, int64_t y_srow, int M, int N, int K, int act_dtype, float* part, int* err,
                       cudaStream_t st);
+bool w8a16_cluster_eligible(int M, int N, int K, int group, int act_dtype);
+int w8a16_cluster_launch(const void* x, int64_t x_srow, const int8_t* w, const void* s, int s_dtype, const void* bias,
+                         void* y, int64_t y_srow, int M, int N, int K, int act_dtype, int* err, cudaStream_t st);
 
 namespace w8 {
 
@@ -313,12 +316,18 @@ static size_t umma_ws_bytes(int M, int N, int K) {
     return align_up(kUmmaPartOffset + w8a16_umma_partial_bytes(M, N, K), 256);
 }
 
-// Kernel choice: the tcgen05 kernel (per-channel scales, M > 16, K % 128 == 0) unless
-// SDB_W8A16_KERNEL=mma forces the register kernel (read per call: tests switch it).
-static bool use_umma(int M, int N, int K, int group) {
+// Kernel choice (per-channel scales, K % 128 == 0): the cluster split-K tcgen05 kernel
+// (w8a16_cluster.cu) for 17 to 128 tokens, the stream-K tcgen05 kernel (w8a16_umma.cu)
+// above 128 tokens, the register kernel up to 16 tokens and for grouped scales.  SDB_W8A16_KERNEL=umma skips the cluster
+// kernel and =mma forces the register kernel (read per call: tests switch it).
+enum class Kern { Cluster, Umma, Mma };
+static Kern choose(int M, int N, int K, int group, int act_dtype) {
     const char* e = getenv("SDB_W8A16_KERNEL");
-    if (e && !strcmp(e, "mma")) return false;
-    return w8a16_umma_eligible(M, N, K, group);
+    if (e && !strcmp(e, "mma")) return Kern::Mma;
+    const bool no_cluster = e && !strcmp(e, "umma");
+    if (!no_cluster && w8a16_cluster_eligible(M, N, K, group, act_dtype)) return Kern::Cluster;
+    if (w8a16_umma_eligible(M, N, K, group)) return Kern::Umma;
+    return Kern::Mma;
 }
 
 template <typename T>
@@ -347,6 +356,7 @@ using namespace sdb;
 extern "C" size_t sdb_w8a16_workspace_size(int M, int N, int K) {
     if (M <= 0 || N <= 0 || K <= 0 || K % w8::KC) return 256;
     size_t total = w8::ws_layout(M, N, K).total;
+    if (K % 128 == 0 && total < w8::kUmmaPartOffset) total = w8::kUmmaPartOffset;  // cluster kernel: error word
     if (w8a16_umma_eligible(M, N, K, 0)) {
         const size_t s = w8::umma_ws_bytes(M, N, K);
         if (s > total) total = s;
@@ -383,7 +393,17 @@ extern "C" int sdb_w8a16_linear(const void* x, int64_t x_srow, const int8_t* qwe
         return SDB_ERR_INVALID_ARG;
     }
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    if (w8::use_umma(M, N, K, group_size)) {
+    const w8::Kern kern = w8::choose(M, N, K, group_size, act_dtype);
+    if (kern == w8::Kern::Cluster) {
+        if (workspace_bytes < w8::kUmmaPartOffset) {
+            set_last_error("workspace too small: need %zu bytes, got %zu", w8::kUmmaPartOffset, workspace_bytes);
+            return SDB_ERR_WORKSPACE;
+        }
+        return w8a16_cluster_launch(x, x_srow, qweight, scale, scale_dtype, bias, y, y_srow, M, N, K, act_dtype,
+                                    reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(workspace) + w8::kUmmaErrOffset),
+                                    st);
+    }
+    if (kern == w8::Kern::Umma) {
         const size_t need = w8::umma_ws_bytes(M, N, K);
         if (workspace_bytes < need) {
             set_last_error("workspace too small: need %zu bytes, got %zu", need, workspace_bytes);

@@ -17,10 +17,12 @@ pytestmark = pytest.mark.gpu
 TOL = dict(rtol=2e-2, atol=2e-3)
 
 
-@pytest.fixture(autouse=True, params=["auto", "mma"])
+@pytest.fixture(autouse=True, params=["auto", "umma", "mma"])
 def kernel_choice(request, monkeypatch):
-    """Every test runs on the default kernel (tcgen05 for M > 16 where the shape allows)
-    and on the register kernel (SDB_W8A16_KERNEL=mma)."""
+    """Every test runs on the default kernel (where the shape allows: the register kernel up
+    to 16 tokens, the cluster split-K tcgen05 kernel for 17 to 128, the stream-K tcgen05
+    kernel above), on the stream-K kernel alone above 16 tokens (SDB_W8A16_KERNEL=umma) and
+    on the register kernel (SDB_W8A16_KERNEL=mma)."""
     if request.param == "auto":
         monkeypatch.delenv("SDB_W8A16_KERNEL", raising=False)
     else:
@@ -74,6 +76,35 @@ def test_cfg3_shapes(pkg, name, M):
     torch.cuda.synchronize()
     assert y.dtype == torch.float16 and y.shape == (M, N)
     _check(y, _ref(x, q, s))
+
+
+@pytest.mark.parametrize("M", [17, 33, 64, 100, 128])
+@pytest.mark.parametrize("N,K", [(6144, 2560), (19456, 2560), (2560, 9728), (203, 384), (1030, 1280)])
+def test_cluster_split_shapes(pkg, M, N, K):
+    """Shapes that give the cluster plan one tile per cluster (6144 x 2560, 2560 x 9728),
+    several tiles per cluster with CTAs spanning tile boundaries (19456 x 2560), a single
+    small cluster (203 x 384) and ragged feature counts (203, 1030: the scalar y tail)."""
+    g = torch.Generator(device="cuda").manual_seed(M * 7 + N)
+    q = torch.randint(-127, 128, (N, K), generator=g, device="cuda", dtype=torch.int32).to(torch.int8)
+    s = (torch.rand(N, generator=g, device="cuda") * 0.01).to(torch.float16)
+    x = torch.randn(M, K, generator=g, device="cuda").to(torch.float16)
+    bias = torch.randn(N, generator=g, device="cuda").to(torch.float16)
+    y = pkg.int8_linear(x, q, s, bias)
+    torch.cuda.synchronize()
+    _check(y, _ref(x, q, s, bias))
+
+
+@pytest.mark.parametrize("width", [2600, 2562])
+def test_strided_output_rows(pkg, width):
+    """y written into a wider buffer: row stride a multiple of 4 (packed 8-byte stores) and not."""
+    from specdec_nanovllm_b200.workloads import cfg3_inputs
+    x, q, s = cfg3_inputs(40, 4096, 2560, seed=11)
+    buf = torch.full((40, width), 7.0, device="cuda", dtype=torch.float16)
+    out = buf[:, :2560]
+    pkg.int8_linear(x, q, s, out=out)
+    torch.cuda.synchronize()
+    _check(out, _ref(x, q, s))
+    assert torch.all(buf[:, 2560:] == 7.0)
 
 
 @pytest.mark.parametrize("M", [3, 40])
