@@ -21,8 +21,10 @@
 //               write y, or an fp32 partial
 // Work: the (feature tile, k tile) space is split evenly over the CTAs; a feature tile
 // cut by a CTA boundary leaves one partial per CTA, summed in slot order by
-// w8a16_umma_merge_kernel (a programmatic dependent launch).  Every wait is bounded
-// and reports SDB_KERR_TIMEOUT.
+// w8a16_umma_merge_kernel (a programmatic dependent launch).  The main kernel is a
+// programmatic dependent launch too: it sets up while the preceding kernel drains and
+// waits (griddepcontrol.wait) before its first load and before it writes.  Every wait is
+// bounded and reports SDB_KERR_TIMEOUT.
 #include <type_traits>
 
 #include "common.cuh"
@@ -138,6 +140,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (lane == 0) {
             prefetch_tensormap(&wmap);
             prefetch_tensormap(&xmap);
+            pdl_wait();  // the preceding kernel (a PDL launch of this one) has completed
             const uint64_t wpol = l2_policy_evict_first();
             const uint64_t xpol = l2_policy_evict_normal();  // every feature tile re-reads x
             Ring r;
@@ -219,6 +222,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     } else {
         // ------------------------------------------------------------- converters / epilogue
         const int ct = threadIdx.x - 64;
+        pdl_wait();  // y and the partials may still be read by the preceding kernel
         const int cr = ct & (FROWS - 1);  // feature row of the tile, 0..127
         const int kh = ct >> 7;           // which 64 k of the tile this thread converts
         const int q = warp & 3;           // TMEM lane quarter of this warp
@@ -308,6 +312,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 // groups of 8), 128 threads = the tile's features.
 template <typename T>
 __global__ void __launch_bounds__(FROWS) w8a16_umma_merge_kernel(const Params p) {
+    pdl_launch_dependents();  // the next call may set up; it waits for this grid itself
     asm volatile("griddepcontrol.wait;" ::: "memory");
     const int ft = blockIdx.x;
     const long long a = (long long)ft * p.KTN;
@@ -418,18 +423,29 @@ int w8a16_umma_launch(const void* x, int64_t x_srow, const int8_t* w, const void
         p.total = g.total;
         p.part = part;
         p.err = err;
+        cudaLaunchConfig_t mcfg = {};
+        mcfg.gridDim = dim3(g.grid, 1, 1);
+        mcfg.blockDim = dim3(w8u::THREADS, 1, 1);
+        mcfg.dynamicSmemBytes = (size_t)g.smem;
+        mcfg.stream = st;
+        cudaLaunchAttribute mattr[1];
+        mattr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        mattr[0].val.programmaticStreamSerializationAllowed = 1;
+        mcfg.attrs = mattr;
+        mcfg.numAttrs = 1;
+        cudaError_t me;
         if (act_dtype == SDB_BF16) {
             auto kern = w8u::w8a16_umma_kernel<__nv_bfloat16>;
             rc = ensure_smem_attr(reinterpret_cast<const void*>(kern), g.smem, 70);
             if (rc) return rc;
-            kern<<<g.grid, w8u::THREADS, g.smem, st>>>(wm, xm, p);
+            me = cudaLaunchKernelEx(&mcfg, kern, wm, xm, p);
         } else {
             auto kern = w8u::w8a16_umma_kernel<__half>;
             rc = ensure_smem_attr(reinterpret_cast<const void*>(kern), g.smem, 71);
             if (rc) return rc;
-            kern<<<g.grid, w8u::THREADS, g.smem, st>>>(wm, xm, p);
+            me = cudaLaunchKernelEx(&mcfg, kern, wm, xm, p);
         }
-        rc = cuda_status(cudaGetLastError(), "w8a16_umma_kernel launch");
+        rc = cuda_status(me, "w8a16_umma_kernel launch");
         if (rc) return rc;
         if (g.grid > 1) {  // some feature tile may be cut by a CTA boundary
             cudaLaunchConfig_t cfg = {};
