@@ -296,21 +296,23 @@ namespace w8 {
 // every call leaves them at 0).
 constexpr int kCounterCap = 65536;  // output tiles
 
-// Split-K partials of the register kernel follow the counter region.
+// Workspace layout shared by the three kernels: split-K counters (register kernel) at a
+// fixed offset with a fixed capacity, then the error word of the tcgen05 kernels (bounded
+// waits report there), then the split-K partials of whichever kernel runs.  Nothing but
+// the tcgen05 kernels' timeouts writes the error word.
+constexpr size_t kUmmaErrOffset = 256 * 1024;  // == align_up(4 * kCounterCap, 256)
+constexpr size_t kUmmaPartOffset = kUmmaErrOffset + 256;
+
 static WsLayout ws_layout(int M, int N, int K) {
     Plan pl = plan(M, N, K);
     WsLayout w;
     w.counters = 0;
-    size_t off = align_up(sizeof(int) * (size_t)kCounterCap, 256);
+    size_t off = kUmmaPartOffset;
     w.part = off;
     if (pl.SK > 1) off = align_up(off + sizeof(float) * (size_t)pl.SK * M * N, 256);
     w.total = off;
     return w;
 }
-
-// The tcgen05 path keeps an error word after the counter region and its partials after that.
-constexpr size_t kUmmaErrOffset = 256 * 1024;  // == align_up(4 * kCounterCap, 256)
-constexpr size_t kUmmaPartOffset = kUmmaErrOffset + 256;
 
 static size_t umma_ws_bytes(int M, int N, int K) {
     return align_up(kUmmaPartOffset + w8a16_umma_partial_bytes(M, N, K), 256);
@@ -356,7 +358,6 @@ using namespace sdb;
 extern "C" size_t sdb_w8a16_workspace_size(int M, int N, int K) {
     if (M <= 0 || N <= 0 || K <= 0 || K % w8::KC) return 256;
     size_t total = w8::ws_layout(M, N, K).total;
-    if (K % 128 == 0 && total < w8::kUmmaPartOffset) total = w8::kUmmaPartOffset;  // cluster kernel: error word
     if (w8a16_umma_eligible(M, N, K, 0)) {
         const size_t s = w8::umma_ws_bytes(M, N, K);
         if (s > total) total = s;

@@ -94,6 +94,27 @@ def test_cluster_split_shapes(pkg, M, N, K):
     _check(y, _ref(x, q, s, bias))
 
 
+@pytest.mark.parametrize("M", [17, 64, 128])
+@pytest.mark.parametrize("scale_dtype", [torch.float32, torch.bfloat16])
+def test_cluster_bf16_activations_scale_dtypes_and_error_word(pkg, M, scale_dtype):
+    """bf16 activations with float32 / bf16 scales and a bias on a shape whose clusters hold
+    several tiles (3 x 2560 -> 6144 is the qkv projection); the kernels' device error word
+    (bounded waits report there) stays clear."""
+    from specdec_nanovllm_b200 import _lib
+    g = torch.Generator(device="cuda").manual_seed(100 + M)
+    N, K = 6144, 2560
+    q = torch.randint(-127, 128, (N, K), generator=g, device="cuda", dtype=torch.int32).to(torch.int8)
+    s = (torch.rand(N, generator=g, device="cuda") * 0.01).to(scale_dtype)
+    x = torch.randn(M, K, generator=g, device="cuda").to(torch.bfloat16)
+    bias = torch.randn(N, generator=g, device="cuda").to(torch.bfloat16)
+    y = pkg.int8_linear(x, q, s, bias)
+    torch.cuda.synchronize()
+    _check(y, _ref(x, q, s, bias))
+    ws = _lib.WORKSPACES.get(x.device, "w8a16", 1)
+    err_word = ws[256 * 1024:256 * 1024 + 4].view(torch.int32).item()  # error word of the tcgen05 kernels
+    assert err_word == 0
+
+
 @pytest.mark.parametrize("width", [2600, 2562])
 def test_strided_output_rows(pkg, width):
     """y written into a wider buffer: row stride a multiple of 4 (packed 8-byte stores) and not."""
