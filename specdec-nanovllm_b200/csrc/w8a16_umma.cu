@@ -6,19 +6,22 @@
 //
 // Transposed so the 128-row tensor-core tile is the feature axis:
 //   Y^T[128 features, N_pad tokens] += W[128 features, 16 k] . X^T[16 k, N_pad tokens]
-// (M = 128, N = tokens padded to a multiple of 16, at most 256 per launch; K = 16 per
-// instruction).  The accumulator lives in TMEM.
+// (M = 128, N = tokens padded to a multiple of 16, at most 256 per launch, more tokens in
+// balanced blocks, 448 = 2 x 224; K = 16 per instruction).  The accumulator (columns
+// 0..N_pad) and the converted A operand (three 64-column buffers from column 256) live in
+// TMEM, so shared memory holds only the raw stages: three of 72 KB at 224 tokens.
 //
 // Per CTA (persistent, one per SM), 320 threads:
 //   warp 0      TMA producer: per 128 k, the 128 x 128 int8 weights as one box (16 KB,
 //               128-byte swizzle) and the matching 128 k of the token rows (two boxes,
 //               128-byte swizzle) into a ring of raw stages
 //   warp 1      TMEM owner and MMA issuer (one thread)
-//   warps 2..9  converters: two threads per feature row (64 k each); int8 -> bf16/f16
-//               exactly, written as the K-major 128-byte-swizzled A operand (2-3 buffers
-//               of 32 KB); after each segment they read the accumulator back (the two
-//               warps of a TMEM lane quarter take alternate 16-token column groups) and
-//               write y, or an fp32 partial
+//   warps 2..9  converters: two threads per feature row (64 k each, the row being the
+//               TMEM lane the warp may access); int8 -> bf16/f16 exactly in registers,
+//               stored to the A buffer with one tcgen05.st (A read by the MMA from TMEM);
+//               after each segment they read the accumulator back (the two warps of a
+//               TMEM lane quarter take alternate 16-token column groups) and write y, or
+//               an fp32 partial
 // Work: the (feature tile, k tile) space is split evenly over the CTAs; a feature tile
 // cut by a CTA boundary leaves one partial per CTA, summed in slot order by
 // w8a16_umma_merge_kernel (a programmatic dependent launch).  The main kernel is a
@@ -37,10 +40,10 @@ namespace w8u {
 constexpr int FROWS = 128;               // features per tile (MMA M)
 constexpr int KT = 128;                  // k per tile (one converter hand-off)
 constexpr int WBOX = FROWS * 64;         // one 64-k box of int8 weights: 8 KB
-constexpr int AHALF = FROWS * 128;       // one 64-k half of the converted tile: 16 KB
-constexpr int ATILE = 2 * AHALF;         // converted tile: 32 KB
-constexpr int MAXNA = 3;                 // converted-tile buffers (3 up to 128 tokens, else 2)
-constexpr int MAXN = 256;                // tokens per launch
+constexpr int MAXNA = 3;                 // converted-tile buffers in TMEM (64 columns each)
+constexpr int MAXN = 256;                // tokens per launch (larger M: balanced blocks)
+constexpr int TMEM_COLS = 512;           // accumulator in columns [0, Npad), A buffers from A_COL
+constexpr int A_COL = 256;
 constexpr int CONV_THREADS = 256;
 constexpr int THREADS = 64 + CONV_THREADS;
 constexpr int kSmemBudget = 224 * 1024;
@@ -107,9 +110,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     bar.accfull = bar.aempty0 + 8 * MAXNA;
     bar.accempty = bar.accfull + 8;
     bar.fin = bar.accempty + 8;
-    uint8_t* araw = smem;               // NA converted tiles (128 k)
-    uint8_t* rraw = smem + NA * ATILE;  // NR raw stages: [W 2 x 8 KB][x 2 x Npad x 128 B]
-    const uint32_t tcols = p.Npad <= 32 ? 32 : (p.Npad <= 64 ? 64 : (p.Npad <= 128 ? 128 : 256));
+    uint8_t* rraw = smem;  // NR raw stages: [W 16 KB][x 2 x Npad x 128 B]
+    const uint32_t tcols = TMEM_COLS;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < NR; ++s) {
@@ -196,13 +198,12 @@ __global__ void __launch_bounds__(THREADS, 1)
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t abase = smem_u32(araw + a.slot * ATILE);
+                    const uint32_t abase = tmem + (uint32_t)(A_COL + a.slot * 64);
                     const uint32_t xbase = smem_u32(rraw + r.slot * p.raw_bytes + 2 * WBOX);
 #pragma unroll
                     for (int ks = 0; ks < KT / 16; ++ks) {
-                        const uint64_t ad = sdesc_sw128(abase + (ks >> 2) * AHALF + (ks & 3) * 32, 16, 1024);
                         const uint64_t bd = sdesc_sw128(xbase + (ks >> 2) * p.xbox + (ks & 3) * 32, 16, 1024);
-                        umma_f16_ss(tmem, ad, bd, idesc, (kt == kt0 && ks == 0) ? 0u : 1u);
+                        umma_f16_ts(tmem, abase + 8 * ks, bd, idesc, (kt == kt0 && ks == 0) ? 0u : 1u);
                     }
                     umma_commit(bar.aempty0 + 8 * a.slot);  // converted tile consumed
                     umma_commit(bar.rempty0 + 8 * r.slot);  // token tile consumed
@@ -221,13 +222,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
     } else {
         // ------------------------------------------------------------- converters / epilogue
-        const int ct = threadIdx.x - 64;
         pdl_wait();  // y and the partials may still be read by the preceding kernel
-        const int cr = ct & (FROWS - 1);  // feature row of the tile, 0..127
-        const int kh = ct >> 7;           // which 64 k of the tile this thread converts
         const int q = warp & 3;           // TMEM lane quarter of this warp
         const uint32_t lane_addr = (uint32_t)(32 * q) << 16;
-        const int row_epi = 32 * q + lane;  // feature row whose accumulator this thread reads
+        const int row_epi = 32 * q + lane;  // feature row this thread converts and reads back
+        const int cr = row_epi;
+        const int kh = (warp - 2) >> 2;   // which 64 k of the tile this thread converts
         const int sw = cr & 7;
         bool ok = true;
         Ring r, a;
@@ -240,25 +240,24 @@ __global__ void __launch_bounds__(THREADS, 1)
             for (int kt = kt0; kt < kt1; ++kt, ++ga) {
                 if (ok && !mbar_wait(bar.rfull0 + 8 * r.slot, r.phase)) ok = false;
                 if (ok && ga >= NA && !mbar_wait(bar.aempty0 + 8 * a.slot, a.phase ^ 1u)) ok = false;
-                // raw row cr: 128 B, 16-byte chunk j (k 16j .. 16j+15) at j ^ (cr & 7);
-                // converted row cr of half kh: 128 B, chunk c at c ^ (cr & 7) (both 128-byte swizzle)
+                // raw row cr: 128 B, 16-byte chunk j (k 16j .. 16j+15) at j ^ (cr & 7); the
+                // 64 converted k of half kh go to TMEM lane cr, 32 columns from A_COL + 64 slot + 32 kh
                 const uint8_t* wr = rraw + r.slot * p.raw_bytes + cr * 128;
-                uint8_t* ar = araw + a.slot * ATILE + kh * AHALF + cr * 128;
                 uint4 v[4];
 #pragma unroll
                 for (int j = 0; j < 4; ++j) v[j] = *reinterpret_cast<const uint4*>(wr + (((4 * kh + j) ^ sw) << 4));
+                uint32_t o[32];
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {  // k 16j .. 16j+15 of this half
-                    uint32_t o[8];
-                    i8x4<T>(v[j].x, o[0], o[1]);
-                    i8x4<T>(v[j].y, o[2], o[3]);
-                    i8x4<T>(v[j].z, o[4], o[5]);
-                    i8x4<T>(v[j].w, o[6], o[7]);
-                    const int c = 2 * j;
-                    *reinterpret_cast<uint4*>(ar + ((c ^ sw) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
-                    *reinterpret_cast<uint4*>(ar + (((c + 1) ^ sw) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
+                    i8x4<T>(v[j].x, o[8 * j + 0], o[8 * j + 1]);
+                    i8x4<T>(v[j].y, o[8 * j + 2], o[8 * j + 3]);
+                    i8x4<T>(v[j].z, o[8 * j + 4], o[8 * j + 5]);
+                    i8x4<T>(v[j].w, o[8 * j + 6], o[8 * j + 7]);
                 }
-                fence_proxy_async_smem();
+                tc_fence_after();
+                tmem_st32(tmem + lane_addr + (uint32_t)(A_COL + a.slot * 64 + 32 * kh), o);
+                tmem_wait_st();
+                tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(bar.afull0 + 8 * a.slot);
                 r.next(NR);
@@ -358,10 +357,10 @@ static Geometry geometry(int Mblk, int N, int K) {
     g.slots = (int)slots;
     g.xbox = g.Npad * 128;
     g.raw_bytes = 2 * WBOX + 2 * g.xbox;  // multiple of 1024: Npad % 16 == 0
-    g.NA = g.Npad <= 128 ? MAXNA : 2;
-    g.NR = (kSmemBudget - g.NA * ATILE) / g.raw_bytes;
+    g.NA = MAXNA;
+    g.NR = kSmemBudget / g.raw_bytes;
     if (g.NR > MAXNR) g.NR = MAXNR;
-    g.smem = g.NA * ATILE + g.NR * g.raw_bytes + 1024;
+    g.smem = g.NR * g.raw_bytes + 1024;
     return g;
 }
 
@@ -393,8 +392,12 @@ int w8a16_umma_launch(const void* x, int64_t x_srow, const int8_t* w, const void
         if (rc) return rc;
     }
     const CUtensorMapDataType dt = act_dtype == SDB_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-    for (int m0 = 0; m0 < M; m0 += w8u::MAXN) {  // token blocks share the partial region in turn
-        const int Mb = M - m0 < w8u::MAXN ? M - m0 : w8u::MAXN;
+    // balanced token blocks of at most MAXN (448 -> 2 x 224: three raw stages fit at 224
+    // tokens, two at 256); they share the partial region in turn
+    const int nblk = (M + w8u::MAXN - 1) / w8u::MAXN;
+    const int Mblk = (M + nblk - 1) / nblk;
+    for (int m0 = 0; m0 < M; m0 += Mblk) {
+        const int Mb = M - m0 < Mblk ? M - m0 : Mblk;
         const w8u::Geometry g = w8u::geometry(Mb, N, K);
         CUtensorMap xm;
         cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)Mb};
