@@ -285,7 +285,7 @@ size_t w8a16_umma_partial_bytes(int M, int N, int K);
 int w8a16_umma_launch(const void* x, int64_t x_srow, const int8_t* w, const void* s, int s_dtype, const void* bias,
                       void* y, int64_t y_srow, int M, int N, int K, int act_dtype, float* part, int* err,
                       cudaStream_t st);
-bool w8a16_cluster_eligible(int M, int N, int K, int group, int act_dtype);
+bool w8a16_cluster_eligible(int M, int N, int K, int group, int act_dtype, bool require_balance);
 int w8a16_cluster_launch(const void* x, int64_t x_srow, const int8_t* w, const void* s, int s_dtype, const void* bias,
                          void* y, int64_t y_srow, int M, int N, int K, int act_dtype, int* err, cudaStream_t st);
 
@@ -318,16 +318,19 @@ static size_t umma_ws_bytes(int M, int N, int K) {
     return align_up(kUmmaPartOffset + w8a16_umma_partial_bytes(M, N, K), 256);
 }
 
-// Kernel choice (per-channel scales, K % 128 == 0): the cluster split-K tcgen05 kernel
-// (w8a16_cluster.cu) for 17 to 128 tokens, the stream-K tcgen05 kernel (w8a16_umma.cu)
-// above 128 tokens, the register kernel up to 16 tokens and for grouped scales.  SDB_W8A16_KERNEL=umma skips the cluster
-// kernel and =mma forces the register kernel (read per call: tests switch it).
+// Kernel choice (per-channel scales, K % 128 == 0): for 17 to 128 tokens the cluster
+// split-K tcgen05 kernel (w8a16_cluster.cu) unless its plan leaves the busiest CTA 3 or
+// more units above an even split (then the stream-K kernel, w8a16_umma.cu); the stream-K
+// kernel above 128 tokens; the register kernel up to 16 tokens and for grouped scales.
+// SDB_W8A16_KERNEL=cluster takes the cluster kernel wherever it has a plan, =umma skips it,
+// =mma forces the register kernel (read per call: tests switch it).
 enum class Kern { Cluster, Umma, Mma };
 static Kern choose(int M, int N, int K, int group, int act_dtype) {
     const char* e = getenv("SDB_W8A16_KERNEL");
     if (e && !strcmp(e, "mma")) return Kern::Mma;
     const bool no_cluster = e && !strcmp(e, "umma");
-    if (!no_cluster && w8a16_cluster_eligible(M, N, K, group, act_dtype)) return Kern::Cluster;
+    const bool any_cluster = e && !strcmp(e, "cluster");
+    if (!no_cluster && w8a16_cluster_eligible(M, N, K, group, act_dtype, !any_cluster)) return Kern::Cluster;
     if (w8a16_umma_eligible(M, N, K, group)) return Kern::Umma;
     return Kern::Mma;
 }

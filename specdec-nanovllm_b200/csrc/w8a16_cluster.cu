@@ -363,7 +363,7 @@ namespace sdb {
 namespace w8c {
 
 struct Geometry {
-    int Npad, FT, KTN, C, G, NW, NX, NA, smem;
+    int Npad, FT, KTN, C, G, NW, NX, NA, smem, umax;
 };
 
 static void rings(int Npad, Geometry& g) {
@@ -442,6 +442,7 @@ static bool plan(int M, int N, int K, bool bf16, Geometry& g) {
             best = cost;
             g.C = C;
             g.G = G;
+            g.umax = (int)u;
         }
     }
     return best >= 0;
@@ -449,10 +450,22 @@ static bool plan(int M, int N, int K, bool bf16, Geometry& g) {
 
 }  // namespace w8c
 
-bool w8a16_cluster_eligible(int M, int N, int K, int group, int act_dtype) {
+// Taken when a resident cluster plan exists and its busiest CTA carries fewer than 3 units
+// more than an even split of all units over the SMs (what the stream-K kernel of
+// w8a16_umma.cu gets).  Measured (B200, 32-128 tokens): the cluster kernel is faster on the
+// Qwen3-4B qkv, o and down projections (busiest CTA 1-2 units above the even split), the
+// stream-K kernel on gate_up (152 feature tiles: 24 units on the busiest CTA against 21),
+// by 3-5 us per call either way.
+// With require_balance false: whenever a resident cluster plan exists.
+bool w8a16_cluster_eligible(int M, int N, int K, int group, int act_dtype, bool require_balance) {
     if (group != 0 || M > w8c::MAXNPAD || K % w8c::KT != 0) return false;
     w8c::Geometry g;
-    return w8c::plan(M, N, K, act_dtype == SDB_BF16, g);
+    if (!w8c::plan(M, N, K, act_dtype == SDB_BF16, g)) return false;
+    if (!require_balance) return true;
+    const long long total = (long long)g.FT * g.KTN;
+    const int sms = device_sm_count();
+    const long long even = (total + sms - 1) / sms;
+    return g.umax - even < 3;
 }
 
 int w8a16_cluster_launch(const void* x, int64_t x_srow, const int8_t* w, const void* s, int s_dtype, const void* bias,

@@ -17,12 +17,13 @@ pytestmark = pytest.mark.gpu
 TOL = dict(rtol=2e-2, atol=2e-3)
 
 
-@pytest.fixture(autouse=True, params=["auto", "umma", "mma"])
+@pytest.fixture(autouse=True, params=["auto", "cluster", "umma", "mma"])
 def kernel_choice(request, monkeypatch):
     """Every test runs on the default kernel (where the shape allows: the register kernel up
-    to 16 tokens, the cluster split-K tcgen05 kernel for 17 to 128, the stream-K tcgen05
-    kernel above), on the stream-K kernel alone above 16 tokens (SDB_W8A16_KERNEL=umma) and
-    on the register kernel (SDB_W8A16_KERNEL=mma)."""
+    to 16 tokens, for 17 to 128 the cluster split-K tcgen05 kernel unless its plan is
+    unbalanced, else and above 128 the stream-K tcgen05 kernel), on the cluster kernel
+    wherever it has a plan (SDB_W8A16_KERNEL=cluster), on the stream-K kernel alone above 16
+    tokens (SDB_W8A16_KERNEL=umma) and on the register kernel (SDB_W8A16_KERNEL=mma)."""
     if request.param == "auto":
         monkeypatch.delenv("SDB_W8A16_KERNEL", raising=False)
     else:
