@@ -347,6 +347,10 @@ int sdb_sample(const void* logits, int64_t logits_stride_row, int dtype,
  *   y     (M, N) act_dtype, y_stride_row
  *   Requires K % 64 == 0; group_size 0 or a multiple of 64 dividing K.
  *   workspace: sdb_w8a16_workspace_size() bytes (split-K partials), zero-filled once.
+ *   Kernels: mma.sync up to 16 tokens and for grouped scales; with per-channel scales
+ *   and K % 128 == 0, tcgen05 above (17-128 tokens: split-K across a thread-block
+ *   cluster where that plan is balanced, else stream-K over persistent CTAs; more
+ *   than 128 tokens: stream-K in token blocks of at most 256).
  * ========================================================================= */
 size_t sdb_w8a16_workspace_size(int M, int N, int K);
 
