@@ -59,7 +59,7 @@ constexpr int CONV_WARP0 = 3;  // warps 0..2: weight producer, MMA issuer, token
 constexpr int THREADS = 32 * CONV_WARP0 + CONV_THREADS;
 constexpr int MAXNPAD = 128;
 constexpr int MAXNW = 14, MAXNX = 8, MAXNA = 3;
-constexpr int RED_TOK = 8;  // tokens per reduction item
+constexpr int RED_TOK = 4;  // tokens per reduction item (4 measured best of 2 / 4 / 8)
 constexpr int MAXC = 8;
 constexpr int kRingBudget = 220 * 1024;
 constexpr int TMEM_COLS = 512;
