@@ -251,7 +251,7 @@ __global__ void __launch_bounds__(THREADS) smp_chunk(const Params p) {
         }
     }
     __syncthreads();
-    // round 2, one list entry per thread: the exact E narrows the list to the columns
+    // second pass, one list entry per thread: the exact E narrows the list to the columns
     // within the band of the best (normally one)
     const int nl = nlive;
     float lb2 = 0.f, ub2 = -1.f;

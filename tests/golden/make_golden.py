@@ -310,9 +310,12 @@ def _load_sampler(root):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("SPECDEC_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("SPECDEC_REFERENCE"),
+                    help="checkout of the reference (or set SPECDEC_REFERENCE)")
     ap.add_argument("--out", default=HERE)
     a = ap.parse_args()
+    if not a.reference:
+        ap.error("give --reference or set SPECDEC_REFERENCE to the reference checkout")
     ref = {
         "attn": _load(a.reference, "ref_paged_decode_attn", "nanovllm/kernels/paged_decode_attn.py"),
         "quant": _load(a.reference, "ref_quant", "nanovllm/layers/quant.py"),
