@@ -48,6 +48,7 @@ constexpr int CONV_THREADS = 256;
 constexpr int THREADS = 64 + CONV_THREADS;
 constexpr int kSmemBudget = 224 * 1024;
 constexpr int MAXNR = 8;
+constexpr int MERGE_TOK = 8;  // tokens per merge thread (4 measured equal, 2 slower)
 
 struct Params {
     const void* s;
@@ -308,7 +309,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
 // Sums the partials of the feature tiles that a CTA boundary cut (slot order, so the
 // result does not depend on timing), then scale and bias.  grid (feature tiles, token
-// groups of 8), 128 threads = the tile's features.
+// groups of MERGE_TOK), 128 threads = the tile's features.
 template <typename T>
 __global__ void __launch_bounds__(FROWS) w8a16_umma_merge_kernel(const Params p) {
     pdl_launch_dependents();  // the next call may set up; it waits for this grid itself
@@ -324,17 +325,17 @@ __global__ void __launch_bounds__(FROWS) w8a16_umma_merge_kernel(const Params p)
     const T* bias = reinterpret_cast<const T*>(p.bias);
     const float bn = bias ? to_f32(bias[n]) : 0.f;
     const float* pt = p.part + (int64_t)ft * p.slots * p.Npad * FROWS + threadIdx.x;
-    const int m0 = blockIdx.y * 8;
-    float v[8];
+    const int m0 = blockIdx.y * MERGE_TOK;
+    float v[MERGE_TOK];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = 0.f;
+    for (int i = 0; i < MERGE_TOK; ++i) v[i] = 0.f;
     for (int s2 = 0; s2 < nseg; ++s2)
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
+        for (int i = 0; i < MERGE_TOK; ++i)
             if (m0 + i < p.M) v[i] += __ldcg(pt + ((int64_t)s2 * p.Npad + m0 + i) * FROWS);
     T* y = reinterpret_cast<T*>(p.y);
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
+    for (int i = 0; i < MERGE_TOK; ++i)
         if (m0 + i < p.M) y[(int64_t)(m0 + i) * p.y_srow + n] = from_f32<T>(v[i] * sc + bn);
 }
 
@@ -452,7 +453,7 @@ int w8a16_umma_launch(const void* x, int64_t x_srow, const int8_t* w, const void
         if (rc) return rc;
         if (g.grid > 1) {  // some feature tile may be cut by a CTA boundary
             cudaLaunchConfig_t cfg = {};
-            cfg.gridDim = dim3(g.FT, (Mb + 7) / 8, 1);
+            cfg.gridDim = dim3(g.FT, (Mb + w8u::MERGE_TOK - 1) / w8u::MERGE_TOK, 1);
             cfg.blockDim = dim3(w8u::FROWS, 1, 1);
             cfg.stream = st;
             cudaLaunchAttribute attr[1];
