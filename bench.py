@@ -5,15 +5,16 @@
 
 Workload (BASELINE configuration 2 at its target point): paged verify attention,
 Qwen3-4B shapes (32 q / 8 kv heads, head_dim 128), k = 6 (7 causal query rows per
-sequence), 64 sequences of 4096 cached tokens per GPU, page 256, scattered block
-tables, bf16, synthetic N(0,1) data.  A step is one kernel pass over the batch.
-Multi-GPU runs shard sequences: every rank owns its own 64 sequences and KV pool
-(weak scaling, no collective on the data path).
+sequence), 64 sequences of 4096 cached tokens, page 256, scattered block tables,
+bf16, synthetic N(0,1) data.  A step is one kernel pass over the batch.  Multi-GPU
+runs shard the 64 sequences over the ranks (strong scaling: 8 per GPU at N = 8),
+each rank with its own KV pool; no collective on the data path.
 
 Metric: HBM GB/s of algorithmic bytes (every visible K/V row once + q in + o out)
-per second, summed over ranks, timed with CUDA events (max over ranks).  One JSON
-line on rank 0.  ``--impl reference`` times the reference's CPU algorithm (the
-oracle restatement of ``paged_decode_attention_ref``) on this host's cores.
+per second for the whole batch, timed with CUDA events around captured graphs of
+steps (max over ranks).  One JSON line on rank 0.  ``--impl reference`` times the
+reference's CPU torch path (``paged_decode_attention_ref`` restated with the k+1
+causal rows, oracle/torch_ref.py) on this host's cores.
 """
 
 from __future__ import annotations
@@ -31,7 +32,7 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-B_PER_GPU, CTX, K_SPEC, PAGE = 64, 4096, 6, 256
+CTX, K_SPEC, PAGE = 4096, 6, 256
 HQ, HKV, D = 32, 8, 128
 N_Q = K_SPEC + 1
 METRIC = "verify-attn HBM GB/s (% of 8 TB/s)"
@@ -119,52 +120,76 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------------------- CPU legs
-def cpu_threads() -> int:
+def cpu_model() -> str:
     try:
-        from threadpoolctl import threadpool_info
-        n = [i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"]
-        return max(n) if n else 1
-    except Exception:
-        return os.cpu_count() or 1
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
 
-def cpu_inputs(seed: int = 0, n_seqs: int = 2):
-    """A host copy of a few sequences of the workload (bf16 values held as float32)."""
-    import numpy as np
-    rng = np.random.default_rng(seed)
+def cpu_case(n_seqs: int, seed: int = 0):
+    """A host copy of ``n_seqs`` sequences of the workload, bf16 like the GPU run."""
+    import torch
+    g = torch.Generator().manual_seed(seed)
     nblk = CTX // PAGE
     nb = n_seqs * nblk
-    k = rng.standard_normal((nb, PAGE, HKV, D), dtype=np.float32)
-    v = rng.standard_normal((nb, PAGE, HKV, D), dtype=np.float32)
-    q = rng.standard_normal((n_seqs * N_Q, HQ, D), dtype=np.float32)
-    bt = rng.permutation(nb).astype(np.int32).reshape(n_seqs, nblk)
-    cl = np.full((n_seqs,), CTX, dtype=np.int32)
+    k = torch.randn(nb, PAGE, HKV, D, generator=g).to(torch.bfloat16)
+    v = torch.randn(nb, PAGE, HKV, D, generator=g).to(torch.bfloat16)
+    q = torch.randn(n_seqs * N_Q, HQ, D, generator=g).to(torch.bfloat16)
+    bt = torch.randperm(nb, generator=g).to(torch.int32).reshape(n_seqs, nblk)
+    cl = torch.full((n_seqs,), CTX, dtype=torch.int32)
     return q, k, v, bt, cl
 
 
-def time_cpu_reference(budget_s: float, steps: int = 1):
-    """Time the oracle restatement of the reference CPU path on (sequence, kv head) pairs.
+def seq_bytes() -> int:
+    """Algorithmic bytes of one sequence of the workload (bf16 K/V rows + q + o)."""
+    return CTX * 2 * HKV * D * 2 + 2 * N_Q * HQ * D * 2
 
-    Returns (GB/s of algorithmic bytes, seconds, pairs per step, description)."""
-    from oracle import attention as oatt
-    q, k, v, bt, cl = cpu_inputs()
-    pairs_all = [(b, h) for b in range(q.shape[0] // N_Q) for h in range(HKV)]
-    oatt.paged_attention_pairs(q, k, v, bt, cl, D ** -0.5, N_Q, pairs_all[:1])      # warm-up
-    t0 = time.perf_counter()
-    oatt.paged_attention_pairs(q, k, v, bt, cl, D ** -0.5, N_Q, pairs_all[:2])
-    per_pair = max((time.perf_counter() - t0) / 2, 1e-4)
-    n_pairs = max(1, min(len(pairs_all), int(budget_s / max(steps, 1) / per_pair)))
-    pairs = [pairs_all[i % len(pairs_all)] for i in range(n_pairs)]
+
+class CpuReference:
+    """The reference's CPU torch path (``paged_decode_attention_ref``, restated in
+    oracle/torch_ref.py with the k+1 causal rows) on this host's cores, one bounded
+    sample of sequences per step."""
+
+    def __init__(self, per_step_s: float):
+        import torch
+        from oracle.torch_ref import paged_attention_torch
+        self.threads = os.cpu_count() or 1
+        torch.set_num_threads(self.threads)
+        self.fn = paged_attention_torch
+        self.data = cpu_case(4)
+        q, k, v, bt, cl = self.data
+        self.run([0])                                   # warm-up
+        t0 = time.perf_counter()
+        self.run([1])
+        per_seq = max(time.perf_counter() - t0, 1e-3)
+        self.n = max(1, min(64, int(per_step_s / per_seq)))
+        self.seqs = [i % 4 for i in range(self.n)]
+
+    def run(self, seqs=None):
+        q, k, v, bt, cl = self.data
+        return self.fn(q, k, v, bt, cl, D ** -0.5, n_q=N_Q, seqs=self.seqs if seqs is None else seqs)
+
+    def describe(self) -> str:
+        return (f"{self.n} sequence(s) of the workload per step (ctx {CTX}, k={K_SPEC}, Qwen3-4B heads, bf16 "
+                f"inputs); torch restatement of paged_decode_attention_ref with the k+1 causal rows, "
+                f"{self.threads} threads, {cpu_model()}")
+
+
+def time_cpu_reference(per_step_s: float, steps: int):
+    """(GB/s, threads, description) of the CPU baseline: median over ``steps`` samples."""
+    ref = CpuReference(per_step_s)
     times = []
     for _ in range(steps):
         t0 = time.perf_counter()
-        oatt.paged_attention_pairs(q, k, v, bt, cl, D ** -0.5, N_Q, pairs)
+        ref.run()
         times.append(time.perf_counter() - t0)
-    bytes_per_pair = CTX * 2 * D * 2 + 2 * N_Q * (HQ // HKV) * D * 2   # bf16 K/V rows + q + o
-    gbs = n_pairs * bytes_per_pair / statistics.median(times) / 1e9
-    desc = (f"{n_pairs} (sequence, kv head) pairs of the workload per step (ctx {CTX}, {N_Q} rows, "
-            f"GQA 4), numpy float32 + BLAS, median of {steps}")
-    return gbs, sum(times), n_pairs, desc
+    gbs = ref.n * seq_bytes() / statistics.median(times) / 1e9
+    return gbs, ref.threads, ref.describe() + f", median of {steps}"
 
 
 # --------------------------------------------------------------------------- reference arm
@@ -172,39 +197,24 @@ def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    budget = 150.0
     total_steps = args.steps + args.warmup
-    per_step_budget = max(0.05, budget / max(total_steps, 1))
-    from oracle import attention as oatt
-    q, k, v, bt, cl = cpu_inputs()
-    pairs_all = [(b, h) for b in range(q.shape[0] // N_Q) for h in range(HKV)]
-    oatt.paged_attention_pairs(q, k, v, bt, cl, D ** -0.5, N_Q, pairs_all[:1])
-    t0 = time.perf_counter()
-    oatt.paged_attention_pairs(q, k, v, bt, cl, D ** -0.5, N_Q, pairs_all[:2])
-    per_pair = max((time.perf_counter() - t0) / 2, 1e-4)
-    n_pairs = max(1, min(len(pairs_all), int(per_step_budget / per_pair)))
-    pairs = [pairs_all[i % len(pairs_all)] for i in range(n_pairs)]
+    ref = CpuReference(per_step_s=max(0.05, 150.0 / max(total_steps, 1)))
     for _ in range(args.warmup):
-        oatt.paged_attention_pairs(q, k, v, bt, cl, D ** -0.5, N_Q, pairs)
+        ref.run()
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        oatt.paged_attention_pairs(q, k, v, bt, cl, D ** -0.5, N_Q, pairs)
+        ref.run()
     dt = time.perf_counter() - t0
-    bytes_per_pair = CTX * 2 * D * 2 + 2 * N_Q * (HQ // HKV) * D * 2
-    gbs = n_pairs * bytes_per_pair * args.steps / dt / 1e9
-    threads = cpu_threads()
-    sample = (f"{n_pairs} (sequence, kv head) pairs per step of the verify workload (ctx {CTX}, "
-              f"k={K_SPEC}, GQA 4); oracle restatement of paged_decode_attention_ref extended to "
-              f"k+1 causal rows, numpy float32 + BLAS")
+    gbs = ref.n * seq_bytes() * args.steps / dt / 1e9
     line = {
         "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(dt / max(args.steps, 1) * 1e3, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"verify-attn B={B_PER_GPU}/GPU ctx={CTX} k={K_SPEC} Qwen3-4B heads",
-                   "global_batch": B_PER_GPU * args.gpus, "seq_len": CTX, "parallelism": "host cores"},
-        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": sample},
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": workload_name(args.global_batch), "global_batch": args.global_batch,
+                   "seq_len": CTX, "k": K_SPEC, "parallelism": "host cores"},
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": ref.threads, "kind": "port",
+                         "sample": ref.describe()},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -212,6 +222,19 @@ def run_reference(args):
 
 
 # --------------------------------------------------------------------------- our arm
+def workload_name(global_batch: int) -> str:
+    return (f"verify-attn B={global_batch} ctx={CTX} k={K_SPEC} (Qwen3-4B heads 32/8, head_dim 128, page {PAGE}), "
+            f"sequences sharded over the GPUs")
+
+
+def graph_len(steps: int, cap: int = 20) -> int:
+    """Steps per captured graph: the largest divisor of ``steps`` up to ``cap``."""
+    for g in range(min(cap, steps), 0, -1):
+        if steps % g == 0:
+            return g
+    return 1
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -225,13 +248,18 @@ def run_ours(args):
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
     pkg = load_package()
     from specdec_nanovllm_b200 import workloads
+    from specdec_nanovllm_b200.partition import shard_range
     from oracle.attention import algorithmic_bytes
 
-    case = workloads.paged_case([CTX] * B_PER_GPU, N_Q, Hq=HQ, Hkv=HKV, D=D, page=PAGE,
-                                dtype=torch.bfloat16, device=dev, seed=1000 + rank,
+    lo, hi = shard_range(args.global_batch, world, rank)
+    B = hi - lo
+    case = workloads.paged_case([CTX] * B, N_Q, Hq=HQ, Hkv=HKV, D=D, page=PAGE,
+                                dtype=torch.bfloat16, device=dev, seed=1000 + lo,
                                 extra_blocks=0, generate_on_device=True)
-    bytes_per_step = algorithmic_bytes([CTX] * B_PER_GPU, N_Q, HQ, HKV, D, 2, 2)
+    bytes_rank = algorithmic_bytes([CTX] * B, N_Q, HQ, HKV, D, 2, 2)
+    bytes_total = algorithmic_bytes([CTX] * args.global_batch, N_Q, HQ, HKV, D, 2, 2)
     out = torch.empty_like(case.q)
+    G = graph_len(args.steps)
 
     def step():
         pkg.paged_attention(case.q, case.k_cache, case.v_cache, case.block_tables, case.cache_seqlens,
@@ -249,8 +277,29 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    # Host cost of one eager call (launches queue behind the GPU, so the wall time of
+    # issuing them is the host's own work per call).
     for _ in range(args.warmup):
         step()
+    torch.cuda.synchronize()
+    n_host = 200
+    t0 = time.perf_counter()
+    for _ in range(n_host):
+        step()
+    host_us = (time.perf_counter() - t0) / n_host * 1e6
+    torch.cuda.synchronize()
+
+    # ---- device timing: G steps per CUDA graph (the reference runs its verify step as a
+    # captured graph, model_runner.py:1257-1310), EXACTLY args.steps steps timed
+    cap = torch.cuda.Stream(dev)
+    cap.wait_stream(torch.cuda.current_stream())
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=cap):
+        for _ in range(G):
+            step()
+    torch.cuda.current_stream().wait_stream(cap)
+    for _ in range(max(1, args.warmup // G)):
+        g.replay()
     barrier()
     sampler = ClockSampler(dev.index)
     sampler.start()
@@ -258,19 +307,20 @@ def run_ours(args):
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     ev0.record()
-    for _ in range(args.steps):
-        step()
+    for _ in range(args.steps // G):
+        g.replay()
     ev1.record()
     barrier()
     clocks = sampler.stop()
     ms = max_over_ranks(ev0.elapsed_time(ev1))
     ms_step = ms / args.steps
-    value = bytes_per_step * world / (ms_step * 1e-3) / 1e9
+    value = bytes_total / (ms_step * 1e-3) / 1e9
+    del g
 
-    # ---- e2e: the public call with pinned host buffers, copies inside the timed region.
-    # Each step copies its own query rows, block table and lengths host->device and reads
-    # its output back device->host; copies run on their own streams, double-buffered, so
-    # step i's copies overlap step i-1's attention as a serving loop would overlap them.
+    # ---- e2e: the public call with pinned host buffers and copies inside the timed region.
+    # Every step copies its query rows, block table and lengths host->device and reads its
+    # output back device->host.  Copies run on their own streams, double-buffered, so step
+    # i's copies overlap step i-1's attention; G such steps are one captured graph.
     q_h = case.q.cpu().pin_memory()
     bt_h = case.block_tables.cpu().pin_memory()
     cl_h = case.cache_seqlens.cpu().pin_memory()
@@ -279,13 +329,11 @@ def run_ours(args):
     bt_d = [torch.empty_like(case.block_tables) for _ in range(2)]
     cl_d = [torch.empty_like(case.cache_seqlens) for _ in range(2)]
     o_d = [torch.empty_like(out) for _ in range(2)]
-    comp = torch.cuda.current_stream()
-    s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
+    comp = torch.cuda.Stream(dev)
+    s_in, s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
     ev_in = [torch.cuda.Event() for _ in range(2)]
     ev_comp = [torch.cuda.Event() for _ in range(2)]
     ev_out = [torch.cuda.Event() for _ in range(2)]
-    for e in ev_comp + ev_out:
-        e.record(comp)
 
     def e2e_step(i):
         j = i & 1
@@ -305,73 +353,89 @@ def run_ours(args):
             out_h[j].copy_(o_d[j], non_blocking=True)
             ev_out[j].record(s_out)
 
-    for i in range(args.warmup):
-        e2e_step(i)
+    def e2e_block():
+        for e in ev_comp + ev_out:
+            e.record(comp)
+        for i in range(G):
+            e2e_step(i)
+        comp.wait_event(ev_out[0])
+        comp.wait_event(ev_out[1])
+
+    comp.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(comp):
+        e2e_block()                              # eager once (sizes nothing new; checks the flow)
+    ge = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(ge, stream=comp):
+        e2e_block()
+    torch.cuda.current_stream().wait_stream(comp)
+    ge.replay()
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(comp)
-    s_in.wait_event(e0)
-    for i in range(args.steps):
-        e2e_step(i)
-    comp.wait_event(ev_out[0])
-    comp.wait_event(ev_out[1])
-    e1.record(comp)
+    e0.record()
+    for _ in range(args.steps // G):
+        ge.replay()
+    e1.record()
     barrier()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1)) / args.steps
-    e2e_val = bytes_per_step * world / (e2e_ms * 1e-3) / 1e9
-    assert torch.equal(out_h[(args.steps - 1) & 1].to(dev), o_d[(args.steps - 1) & 1])
+    e2e_val = bytes_total / (e2e_ms * 1e-3) / 1e9
+    last = (G - 1) & 1
+    assert torch.equal(out_h[last].to(dev), o_d[last])
     h2d = q_h.numel() * q_h.element_size() + bt_h.numel() * 4 + cl_h.numel() * 4
     d2h = out_h[0].numel() * out_h[0].element_size()
+    del ge
 
-    # ---- memory-floor twin (same grid and TMA stream, no math), outside the timed region
+    # ---- memory-floor twin (same TMA stream, no math), outside the timed region
     ro_ws = pkg.paged_attention_readonly(case.q, case.k_cache, case.v_cache, case.block_tables,
                                          case.cache_seqlens, n_q=N_Q)
     r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    n_ro = max(10, min(args.steps, 200))
+    n_ro = 50
     r0.record()
     for _ in range(n_ro):
         pkg.paged_attention_readonly(case.q, case.k_cache, case.v_cache, case.block_tables,
                                      case.cache_seqlens, n_q=N_Q, workspace=ro_ws)
     r1.record()
     torch.cuda.synchronize()
-    kv_bytes = CTX * B_PER_GPU * 2 * HKV * D * 2
+    kv_bytes = CTX * B * 2 * HKV * D * 2
     ro_gbs = kv_bytes / (r0.elapsed_time(r1) / n_ro * 1e-3) / 1e9
 
     peak, peak_kind = measured_peak()
-    per_launch_gbs = bytes_per_step / (ms_step * 1e-3) / 1e9
-    workload = f"verify-attn B={B_PER_GPU} ctx={CTX} k={K_SPEC}"
-    traffic = committed_traffic(workload)
-    splits = pkg.attention.default_splits(B_PER_GPU, N_Q, HQ, HKV, D, PAGE, CTX // PAGE, torch.bfloat16)
-    launches_per_step = 1 if splits == 1 else 2  # attention (+ the split merge)
+    per_gpu_gbs = bytes_rank / (ms_step * 1e-3) / 1e9
+    traffic = committed_traffic(f"verify-attn B={B} ctx={CTX} k={K_SPEC}")
+    kind, slots, _ = pkg.attention.plan(B, N_Q, HQ, HKV, D, PAGE, CTX // PAGE, torch.bfloat16)
+    merge = slots > 1
+    launches_per_step = 2 if merge else 1  # attention (+ the split merge)
 
     cpu = None
     if world == 1 and rank == 0 and not args.skip_cpu:
-        gbs, secs, n_pairs, desc = time_cpu_reference(budget_s=12.0, steps=3)
-        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": cpu_threads(), "kind": "port",
-               "sample": desc}
+        gbs, threads, desc = time_cpu_reference(per_step_s=4.0, steps=3)
+        cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port", "sample": desc}
 
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 5),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic",
-            "config": {"workload": f"{workload} (Qwen3-4B heads 32/8, head_dim 128, page {PAGE}) per GPU",
-                       "global_batch": B_PER_GPU * world, "seq_len": CTX, "k": K_SPEC,
-                       "parallelism": f"seq-shard{world}", "splits": splits,
-                       "l2": "no flush: 1.07 GB of KV per GPU per step exceeds the 126 MB L2",
-                       "bytes_per_step_per_gpu": bytes_per_step},
-            "pct_of_8tbs": round(100.0 * per_launch_gbs / 8000.0, 2),
-            "roofline": {"bound": "hbm", "achieved": round(per_launch_gbs, 2), "peak": peak,
+            "config": {"workload": workload_name(args.global_batch), "global_batch": args.global_batch,
+                       "seqs_per_gpu": B, "seq_len": CTX, "k": K_SPEC,
+                       "parallelism": f"seq-shard{world}", "plan": f"{kind} x{slots}",
+                       "graph_steps": G,
+                       "l2": f"no flush: {kv_bytes / 1e9:.2f} GB of KV per GPU per step exceeds the 126 MB L2"
+                             if kv_bytes > 126e6 else "KV per GPU fits L2: steps re-read it from L2",
+                       "bytes_per_step": bytes_total, "bytes_per_step_per_gpu": bytes_rank},
+            "pct_of_8tbs": round(100.0 * per_gpu_gbs / 8000.0, 2),
+            "roofline": {"bound": "hbm", "achieved": round(per_gpu_gbs, 2), "peak": peak,
                          "peak_kind": peak_kind, "unit": "GB/s",
-                         "frac": round(per_launch_gbs / peak, 4),
+                         "frac": round(per_gpu_gbs / peak, 4),
                          "traffic": traffic, "kernel": "pa_umma_kernel",
-                         "achieved_over": "whole step (pa_umma_kernel + pa_umma_merge_kernel)",
+                         "achieved_over": "whole step per GPU (pa_umma_kernel + pa_umma_merge_kernel)"
+                                          if merge else "whole step per GPU (pa_umma_kernel)",
                          "readonly_floor_gbs": round(ro_gbs, 2)},
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 5),
-                    "copies": "pinned host, own streams, double-buffered"},
+                    "copies": f"pinned host, own streams, double-buffered; {G} steps per captured graph"},
+            "host_us_per_call": round(host_us, 1),
             "gpu_launches": args.steps * launches_per_step,
             "clocks": clocks,
         }
@@ -380,7 +444,6 @@ def run_ours(args):
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
     return 0
-
 
 
 # --------------------------------------------------------------------------- side modes
@@ -512,9 +575,41 @@ def run_side(args):
                              "unit": "GB/s", "frac": round(gbs / peak, 4),
                              "note": "issue-bound: the Philox noise of every column is most of the instructions"},
                 "gpu_launches": 2 * steps}
+    elif args.mode == "attn_sweep":
+        # the cfg2 grid: verify (k=6) and decode over B x ctx, one line with a row per point
+        from oracle.attention import algorithmic_bytes
+        rows = []
+        for n_q in (N_Q, 1):
+            for B in (1, 8, 32, 64):
+                for L in (512, 2048, 4096):
+                    # cases that fit L2 rotate over copies (>= 256 MB together), so every call reads HBM
+                    kv = B * L * 2 * HKV * D * 2
+                    n_cp = min(128, -(-256_000_000 // kv))
+                    cases = [workloads.paged_case([L] * B, n_q, device="cuda", seed=B + L + 97 * c, extra_blocks=0,
+                                                  generate_on_device=True, **workloads.QWEN3_4B)
+                             for c in range(n_cp)]
+                    out = torch.empty_like(cases[0].q)
+                    ctr = [0]
+
+                    def fn(cases=cases, out=out, n_q=n_q):
+                        c = cases[ctr[0] % len(cases)]
+                        ctr[0] += 1
+                        pkg.paged_attention(c.q, c.k_cache, c.v_cache, c.block_tables, c.cache_seqlens, c.scale,
+                                            n_q=n_q, out=out)
+                    ms = _time_events(fn, steps, args.warmup, per_graph=max(20, n_cp))
+                    nbytes = algorithmic_bytes([L] * B, n_q, HQ, HKV, D, 2, 2)
+                    kind, slots, _ = pkg.attention.plan(B, n_q, HQ, HKV, D, PAGE, L // PAGE, torch.bfloat16)
+                    gbs = nbytes / (ms * 1e-3) / 1e9
+                    rows.append({"n_q": n_q, "B": B, "ctx": L, "us": round(ms * 1e3, 2), "GB/s": round(gbs, 1),
+                                 "frac": round(gbs / peak, 3), "plan": f"{kind} x{slots}",
+                                 "copies": n_cp})
+                    del cases, out
+        line = {"metric": "attention cfg2 sweep", "unit": "GB/s", "n_gpus": 1, "steps": steps,
+                "warmup": args.warmup, "dtype": "bf16", "data": "synthetic", "peak": peak, "peak_kind": peak_kind,
+                "rows": rows}
     else:  # decode attention
         from oracle.attention import algorithmic_bytes
-        B, L = B_PER_GPU, CTX
+        B, L = 64, CTX
         case = workloads.paged_case([L] * B, 1, device="cuda", seed=3, extra_blocks=0, generate_on_device=True,
                                     **workloads.QWEN3_4B)
         out = torch.empty_like(case.q)
@@ -537,11 +632,13 @@ def run_side(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=4000)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--global-batch", type=int, default=64,
+                    help="sequences of the whole job, sharded over the GPUs (strong scaling)")
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--skip-cpu", action="store_true", help="omit the CPU baseline leg")
-    ap.add_argument("--mode", choices=["verify_attn", "decode_attn", "verify_batch", "w8a16", "sample"],
+    ap.add_argument("--mode", choices=["verify_attn", "decode_attn", "attn_sweep", "verify_batch", "w8a16", "sample"],
                     default="verify_attn", help="verify_attn is the headline; the others measure the "
                     "secondary kernels of the path on one GPU")
     ap.add_argument("--m", type=int, default=1, help="tokens (M) for --mode w8a16")

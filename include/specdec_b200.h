@@ -89,6 +89,21 @@ size_t sdb_paged_attention_workspace_size(int B, int n_q, int Hq, int Hkv, int D
 int sdb_paged_attention_default_splits(int B, int n_q, int Hq, int Hkv, int D, int page,
                                        int max_blocks, int dtype);
 
+/* The decomposition sdb_paged_attention launches for this static shape and `splits`
+ * (0 = default), without launching: *kernel receives one of SDB_ATTN_PLAN_* (-1 for
+ * invalid sizes), *slots the partial slots per (sequence, kv head) the launch uses (the
+ * strided split count, or the slots of the grouped partition); returns the workspace
+ * bytes that launch needs (0 for invalid sizes).  Follows the same kernel choice as the
+ * launch (SDB_ATTN_KERNEL=mma included).  Host only: no CUDA call beyond the SM count.
+ * The reference has no counterpart (its split count is a call argument,
+ * nanovllm/kernels/paged_decode_attn_cuda.py:52). */
+#define SDB_ATTN_PLAN_CUDA_CORE        0  /* fp32 / other shapes: one CTA per (kv head, seq) */
+#define SDB_ATTN_PLAN_MMA              1  /* mma.sync kernel, `slots` key chunks per pair    */
+#define SDB_ATTN_PLAN_TCGEN05_STRIDED  2  /* tcgen05 kernel, `slots` key chunks per pair     */
+#define SDB_ATTN_PLAN_TCGEN05_GROUPED  3  /* tcgen05 kernel, balanced partition over groups  */
+size_t sdb_paged_attention_plan(int B, int n_q, int Hq, int Hkv, int D, int page, int max_blocks,
+                                int dtype, int splits, int* kernel, int* slots);
+
 int sdb_paged_attention(const void* q, int64_t q_stride_row, int64_t q_stride_head,
                         const void* k_cache, const void* v_cache,
                         int64_t kv_stride_block, int64_t kv_stride_page, int64_t kv_stride_head,
@@ -108,11 +123,13 @@ int sdb_paged_attention(const void* q, int64_t q_stride_row, int64_t q_stride_he
  * Same arguments as sdb_paged_attention without the workspace: the split
  * partials and merge counters live in a file-scope device array of
  * SDB_NOALLOC_SCRATCH_BYTES that every GPU loading the library holds until the
- * process exits.  Shapes needing more scratch return SDB_ERR_WORKSPACE before any
- * launch.  The first call on a device (that device current) looks the array up
- * and clears its counters on the given stream; make it before anything that must
- * not see that set-up.  All calls share the array: calls that overlap on the GPU
- * race and must be serialised by the caller.  Allocates nothing. */
+ * process exits.  Shapes needing more scratch (sized for the split count the launch
+ * actually uses, see sdb_paged_attention_plan) return SDB_ERR_WORKSPACE before any
+ * launch.  The first call on a device (that device current) looks the array up and
+ * clears its error word and counters with cudaMemsetAsync on the given stream; that
+ * first call must not be made while the stream is being captured into a CUDA graph
+ * (it returns SDB_ERR_INVALID_ARG if it is).  All calls share the array: calls that
+ * overlap on the GPU race and must be serialised by the caller.  Allocates nothing. */
 #define SDB_NOALLOC_SCRATCH_BYTES (16u << 20)
 int sdb_paged_attention_noalloc(const void* q, int64_t q_stride_row, int64_t q_stride_head,
                                 const void* k_cache, const void* v_cache,
@@ -123,6 +140,15 @@ int sdb_paged_attention_noalloc(const void* q, int64_t q_stride_row, int64_t q_s
                                 int B, int n_q, int Hq, int Hkv, int D, int page,
                                 int max_blocks, int num_blocks,
                                 float softmax_scale, int dtype, int splits, void* stream);
+
+/* The error word of sdb_paged_attention_noalloc on the current device (no counterpart
+ * in the reference).  Those callers have no workspace, so this is how they see the
+ * SDB_KERR_* bits the kernels record (a clamped block id, a clamped cache length, a
+ * bounded wait that gave up).  Enqueues on `stream` a 4-byte copy of the word into
+ * *host_word (valid once the stream has synchronised; pinned or pageable memory)
+ * and, with clear != 0, then resets the word to 0.  The bits otherwise accumulate
+ * over every call on the device.  Allocates nothing. */
+int sdb_paged_attention_noalloc_error_word(int32_t* host_word, int clear, void* stream);
 
 /* Memory-floor twin of sdb_paged_attention: the same grid, the same TMA loads
  * of every visible K/V tile, no math; writes one checksum word per CTA into the

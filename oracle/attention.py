@@ -51,26 +51,31 @@ def paged_attention(q, k_cache, v_cache, block_tables, cache_seqlens, scale,
     assert Hq % Hkv == 0
     rep = Hq // Hkv
     out = np.zeros((total, Hq, D), dtype=compute_dtype)
+    # row r of n sees keys [0, visible_keys(L, n, r)); the rest are masked to -inf
     for b in range(B):
         L = int(cache_seqlens[b])
         if L <= 0:
             continue                                   # zeros (paged_decode_attn.py:480-482)
         nblk = (L + page - 1) // page
         phys = block_tables[b, :nblk].astype(np.int64)
-        k = k_cache[phys].reshape(-1, Hkv, D)[:L].astype(compute_dtype)
+        k = k_cache[phys].reshape(-1, Hkv, D)[:L].astype(compute_dtype)   # (L, Hkv, D)
         v = v_cache[phys].reshape(-1, Hkv, D)[:L].astype(compute_dtype)
-        k = np.repeat(k, rep, axis=1)                  # (L, Hq, D), like repeat_interleave
-        v = np.repeat(v, rep, axis=1)
-        for r in range(n_q):
-            nv = visible_keys(L, n_q, r)
-            if nv == 0:
-                continue
-            qr = q[b * n_q + r].astype(compute_dtype)  # (Hq, D)
-            logits = np.einsum("hd,lhd->hl", qr, k[:nv]) * compute_dtype(scale)
-            logits = logits - logits.max(axis=-1, keepdims=True)
-            p = np.exp(logits)
-            p = p / p.sum(axis=-1, keepdims=True)
-            out[b * n_q + r] = np.einsum("hl,lhd->hd", p, v[:nv])
+        nv = np.array([visible_keys(L, n_q, r) for r in range(n_q)])
+        cols = np.arange(L)
+        masked = cols[None, :] >= nv[:, None]                             # (n_q, L)
+        qb = q[b * n_q:(b + 1) * n_q].astype(compute_dtype)               # (n_q, Hq, D)
+        for h in range(Hkv):
+            # the GQA group of kv head h (repeat_interleave order, :484-485): q heads h*rep ..
+            qg = qb[:, h * rep:(h + 1) * rep].reshape(n_q * rep, D)
+            logits = (qg @ k[:, h].T).reshape(n_q, rep, L) * compute_dtype(scale)
+            logits = np.where(masked[:, None, :], -np.inf, logits)
+            mx = logits.max(axis=-1, keepdims=True)
+            mx = np.where(np.isfinite(mx), mx, 0.0)
+            p = np.exp(logits - mx)
+            den = p.sum(axis=-1, keepdims=True)
+            p = p / np.where(den > 0, den, 1.0)                          # rows that see no key stay 0
+            out[b * n_q:(b + 1) * n_q, h * rep:(h + 1) * rep] = (p.reshape(n_q * rep, L) @ v[:, h]).reshape(
+                n_q, rep, D)
     return out
 
 

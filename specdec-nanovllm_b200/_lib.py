@@ -26,6 +26,9 @@ SDB_KERR_BLOCK_ID = 0x2
 SDB_KERR_TIMEOUT = 0x4
 SDB_KERR_TOKEN = 0x8
 
+# decomposition of an attention launch (sdb_paged_attention_plan)
+ATTN_PLAN_NAMES = {0: "cuda_core", 1: "mma", 2: "tcgen05_strided", 3: "tcgen05_grouped"}
+
 SDB_F32, SDB_BF16, SDB_F16 = 0, 1, 2
 DTYPE_CODE = {torch.float32: SDB_F32, torch.bfloat16: SDB_BF16, torch.float16: SDB_F16}
 
@@ -52,6 +55,7 @@ SIGNATURES = {
     "sdb_build_info": (ctypes.c_char_p, []),
     "sdb_paged_attention_workspace_size": (_c_sz, [_c_i32] * 6),
     "sdb_paged_attention_default_splits": (_c_i32, [_c_i32] * 8),
+    "sdb_paged_attention_plan": (_c_sz, [_c_i32] * 9 + [_c_p, _c_p]),
     "sdb_paged_attention": (_c_i32, [
         _c_p, _c_i64, _c_i64, _c_p, _c_p, _c_i64, _c_i64, _c_i64, _c_p, _c_i64, _c_p,
         _c_p, _c_i64, _c_i64, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32,
@@ -65,6 +69,7 @@ SIGNATURES = {
         _c_p, _c_i64, _c_i64, _c_p, _c_p, _c_i64, _c_i64, _c_i64, _c_p, _c_i64, _c_p,
         _c_p, _c_i64, _c_i64, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32,
         _c_f32, _c_i32, _c_i32, _c_p]),
+    "sdb_paged_attention_noalloc_error_word": (_c_i32, [_c_p, _c_i32, _c_p]),
     "sdb_paged_attention_readonly": (_c_i32, [
         _c_p, _c_i64, _c_i64, _c_p, _c_p, _c_i64, _c_i64, _c_i64, _c_p, _c_i64, _c_p,
         _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32,

@@ -49,6 +49,19 @@ def default_splits(B, n_q, Hq, Hkv, D, page, max_blocks, dtype: torch.dtype) -> 
         B, n_q, Hq, Hkv, D, page, max_blocks, _lib.DTYPE_CODE[dtype]))
 
 
+def plan(B, n_q, Hq, Hkv, D, page, max_blocks, dtype: torch.dtype, splits: int = 0):
+    """(kernel, partial slots per pair, workspace bytes) of the launch ``paged_attention``
+    makes for this static shape: kernel is one of "tcgen05_strided", "tcgen05_grouped",
+    "mma" or "cuda_core" (host-side query, no launch)."""
+    import ctypes
+    k, s = ctypes.c_int(-1), ctypes.c_int(0)
+    need = _lib.lib().sdb_paged_attention_plan(B, n_q, Hq, Hkv, D, page, max_blocks, _lib.DTYPE_CODE[dtype],
+                                               splits, ctypes.byref(k), ctypes.byref(s))
+    if k.value < 0:
+        raise ValueError("invalid attention shape")
+    return _lib.ATTN_PLAN_NAMES[k.value], int(s.value), int(need)
+
+
 def paged_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                     block_tables: torch.Tensor, cache_seqlens: torch.Tensor, softmax_scale: float,
                     n_q: int = 1, splits: int = 0, out: torch.Tensor | None = None,

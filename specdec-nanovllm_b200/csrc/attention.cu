@@ -668,6 +668,20 @@ static int pick_splits(int B, int R, int Hkv, int page, int max_blocks, int sms)
     return best;
 }
 
+// Split count and key chunk the mma.sync path launches for a requested `splits`
+// (0: its default): at most kMaxSplits, and no split that can never hold a key.
+static int mma_launch_splits(int B, int R, int Hkv, int page, int max_blocks, int splits, long long* chunk_out) {
+    if (splits <= 0) splits = pick_splits(B, R, Hkv, page, max_blocks, device_sm_count());
+    // the last-CTA merge keeps splits x R coefficients in the (idle) stage ring
+    if (splits > kMaxSplits) splits = kMaxSplits;
+    const long long max_ctx = (long long)max_blocks * page;
+    long long chunk = ((max_ctx + splits - 1) / splits + BN - 1) / BN * BN;
+    if (chunk < BN) chunk = BN;
+    splits = (int)((max_ctx + chunk - 1) / chunk);
+    *chunk_out = chunk;
+    return splits < 1 ? 1 : splits;
+}
+
 }  // namespace attn
 }  // namespace sdb
 
@@ -703,6 +717,33 @@ extern "C" size_t sdb_paged_attention_workspace_size(int B, int n_q, int Hq, int
 
 extern "C" const int32_t* sdb_paged_attention_error_word(const void* workspace, int, int, int, int, int, int) {
     return reinterpret_cast<const int32_t*>(workspace);
+}
+
+extern "C" size_t sdb_paged_attention_plan(int B, int n_q, int Hq, int Hkv, int D_, int page, int max_blocks,
+                                           int dtype, int splits, int* kernel, int* slots) {
+    int k = -1, s = 0;
+    size_t need = 0;
+    if (B > 0 && n_q > 0 && Hkv > 0 && Hq > 0 && Hq % Hkv == 0 && page > 0 && max_blocks > 0 && D_ > 0) {
+        const int R = n_q * (Hq / Hkv);
+        if (umma_path(dtype, D_, page, R) && prefer_umma()) {
+            const UmmaShape u = umma_launch_shape(B, Hkv, page, max_blocks, splits);
+            k = u.grouped ? SDB_ATTN_PLAN_TCGEN05_GROUPED : SDB_ATTN_PLAN_TCGEN05_STRIDED;
+            s = u.slots;
+            need = ws_layout(B, R, Hkv, s).total;
+        } else if (mma_path(dtype, D_, page, R)) {
+            long long chunk = 0;
+            k = SDB_ATTN_PLAN_MMA;
+            s = mma_launch_splits(B, R, Hkv, page, max_blocks, splits, &chunk);
+            need = ws_layout(B, R, Hkv, s).total;
+        } else {
+            k = SDB_ATTN_PLAN_CUDA_CORE;
+            s = 1;
+            need = ws_layout(B, R, Hkv, 1).err + 256;
+        }
+    }
+    if (kernel) *kernel = k;
+    if (slots) *slots = s;
+    return need;
 }
 
 namespace {
@@ -906,14 +947,8 @@ int attention_impl(const void* q, int64_t q_srow, int64_t q_shead, const void* k
     }
 
     if (mma_path(dtype, D_, page, R)) {
-        if (splits <= 0) splits = pick_splits(B, R, Hkv, page, max_blocks, device_sm_count());
-        // the last-CTA merge keeps splits x R coefficients in the (idle) stage ring
-        if (splits > kMaxSplits) splits = kMaxSplits;
-        const long long max_ctx = (long long)max_blocks * page;
-        long long chunk = ((max_ctx + splits - 1) / splits + BN - 1) / BN * BN;
-        if (chunk < BN) chunk = BN;
-        splits = (int)((max_ctx + chunk - 1) / chunk);  // drop splits that can never hold a key
-        if (splits < 1) splits = 1;
+        long long chunk = 0;
+        splits = mma_launch_splits(B, R, Hkv, page, max_blocks, splits, &chunk);
         if ((long long)B * Hkv > kCounterCap) {
             set_last_error("B * Hkv = %lld exceeds the supported %d (sequence, kv head) pairs", (long long)B * Hkv,
                            kCounterCap);
@@ -1016,12 +1051,8 @@ extern "C" int sdb_paged_attention_readonly(const void* q, int64_t q_srow, int64
         set_last_error("read-only twin exists for the tensor-core path only");
         return SDB_ERR_UNSUPPORTED;
     }
-    if (splits <= 0) splits = pick_splits(B, R, Hkv, page, max_blocks, device_sm_count());
-    if (splits > kMaxSplits) splits = kMaxSplits;
-    const long long max_ctx = (long long)max_blocks * page;
-    long long chunk = ((max_ctx + splits - 1) / splits + BN - 1) / BN * BN;
-    if (chunk < BN) chunk = BN;
-    splits = (int)((max_ctx + chunk - 1) / chunk);
+    long long chunk = 0;
+    splits = mma_launch_splits(B, R, Hkv, page, max_blocks, splits, &chunk);
     WsLayout w = ws_layout(B, R, Hkv, splits);
     const size_t need = w.total + align_up(sizeof(unsigned) * (size_t)B * Hkv * splits, 256);
     if (workspace_bytes < need) {

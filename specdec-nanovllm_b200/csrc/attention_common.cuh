@@ -83,6 +83,14 @@ SDB_DEV int load_len(const Params& p, int b) {
 // tcgen05 path (csrc/attention_umma.cu)
 bool umma_path(int dtype, int D_, int page, int R);
 int pick_umma_splits(int B, int R, int Hkv, int page, int max_blocks, int sms);
+// The decomposition a tcgen05 launch takes: the grouped partition (flat_T / flat_total /
+// groups set) or strided key chunks of `chunk` keys; `slots` partials per pair either way.
+struct UmmaShape {
+    bool grouped;
+    int slots, chunk, flat_T, groups;
+    long long flat_total;
+};
+UmmaShape umma_launch_shape(int B, int Hkv, int page, int max_blocks, int splits);
 int launch_umma(const void* k_cache, const void* v_cache, int dtype, int64_t sb, int64_t sp, int64_t sh,
                 Params& p, void* workspace, size_t workspace_bytes, int splits, cudaStream_t st);
 

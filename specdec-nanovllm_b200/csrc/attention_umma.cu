@@ -923,33 +923,52 @@ int pick_umma_splits(int B, int, int Hkv, int page, int max_blocks, int sms) {
     return umma_plan(B, Hkv, page, max_blocks, sms).splits;
 }
 
-// `splits` is the partial-slot capacity per pair.  The grouped partition runs when the
-// plan prefers it and the capacity covers it; otherwise every pair is split into
-// `splits` key chunks, strided over the persistent CTAs.
+// The launch decomposition for a `splits` capacity (0: the plan's default).  The grouped
+// partition runs when the plan prefers it and the capacity covers it, and then uses
+// exactly the slots a pair can straddle; otherwise every pair is split into `splits`
+// key chunks (at most kMaxUmmaSplits, dropping chunks that can hold no key).
+UmmaShape umma_launch_shape(int B, int Hkv, int page, int max_blocks, int splits) {
+    const int sms = device_sm_count();
+    const FlatShape fs = flat_shape(B, Hkv, page, max_blocks, sms);
+    const UmmaPlan plan = umma_plan(B, Hkv, page, max_blocks, sms);
+    if (splits <= 0) splits = plan.splits;
+    UmmaShape u{};
+    if (plan.grouped && splits >= fs.slots && fs.total < (1LL << 31)) {
+        u.grouped = true;
+        u.slots = fs.slots;
+        u.flat_T = fs.T;
+        u.flat_total = fs.total;
+        u.groups = fs.groups;
+        return u;
+    }
+    if (splits > umma::kMaxUmmaSplits) splits = umma::kMaxUmmaSplits;
+    const long long max_ctx = (long long)max_blocks * page;
+    long long chunk = ((max_ctx + splits - 1) / splits + umma::UBN - 1) / umma::UBN * umma::UBN;
+    if (chunk < umma::UBN) chunk = umma::UBN;
+    splits = (int)((max_ctx + chunk - 1) / chunk);
+    u.grouped = false;
+    u.slots = splits < 1 ? 1 : splits;
+    u.chunk = (int)chunk;
+    return u;
+}
+
 int launch_umma(const void* k_cache, const void* v_cache, int dtype, int64_t sb, int64_t sp, int64_t sh,
                 Params& p, void* workspace, size_t workspace_bytes, int splits, cudaStream_t st) {
     const int sms = device_sm_count();
-    const FlatShape fs = flat_shape(p.B, p.Hkv, p.page, p.max_blocks, sms);
-    const UmmaPlan plan = umma_plan(p.B, p.Hkv, p.page, p.max_blocks, sms);
-    if (splits <= 0) splits = plan.splits;
+    const UmmaShape u = umma_launch_shape(p.B, p.Hkv, p.page, p.max_blocks, splits);
+    splits = u.slots;
     int grid;
     bool merge;
-    if (plan.grouped && splits >= fs.slots && fs.total < (1LL << 31)) {
-        p.flat_T = fs.T;
-        p.flat_total = fs.total;
-        p.flat_grid = fs.groups;
+    if (u.grouped) {
+        p.flat_T = u.flat_T;
+        p.flat_total = u.flat_total;
+        p.flat_grid = u.groups;
         p.chunk = 0;
-        grid = fs.groups * p.Hkv;
-        merge = fs.groups > 1;
+        grid = u.groups * p.Hkv;
+        merge = u.groups > 1;
     } else {
-        if (splits > umma::kMaxUmmaSplits) splits = umma::kMaxUmmaSplits;
-        const long long max_ctx = (long long)p.max_blocks * p.page;
-        long long chunk = ((max_ctx + splits - 1) / splits + umma::UBN - 1) / umma::UBN * umma::UBN;
-        if (chunk < umma::UBN) chunk = umma::UBN;
-        splits = (int)((max_ctx + chunk - 1) / chunk);
-        if (splits < 1) splits = 1;
         p.flat_T = 0;
-        p.chunk = (int)chunk;
+        p.chunk = u.chunk;
         const long long items = (long long)p.B * p.Hkv * splits;
         grid = (int)(items < sms ? items : sms);
         merge = splits > 1;

@@ -82,11 +82,61 @@ def test_cfg1_decode_fp32(pkg, W):
     _check(out, _oracle(case), FP32_TOL)
 
 
-@pytest.mark.parametrize("B,ctx", [(1, 512), (8, 512), (8, 2048), (1, 4096)])
+_CFG2_CACHE = {}
+
+
+def _cfg2_case_and_oracle(W, B, ctx, n_q):
+    """Inputs and float64 oracle output of one cfg2 point, shared by both kernel choices."""
+    key = (B, ctx, n_q)
+    if key not in _CFG2_CACHE:  # all 24 points together hold about 6 GB of device memory
+        lens = W.cfg2_lens(B, ctx, seed=B + ctx)
+        case = W.paged_case(lens, n_q, seed=ctx + n_q, max_blocks=ctx // 256, generate_on_device=B >= 32,
+                            **W.QWEN3_4B)
+        _CFG2_CACHE[key] = (case, _oracle(case))
+    return _CFG2_CACHE[key]
+
+
+@pytest.mark.parametrize("ctx", [512, 2048, 4096])
+@pytest.mark.parametrize("B", [1, 8, 32, 64])
 @pytest.mark.parametrize("n_q", [7, 1])
-def test_cfg2_verify_and_decode(pkg, W, B, ctx, n_q):
-    lens = W.cfg2_lens(B, ctx, seed=B + ctx)
-    case = W.paged_case(lens, n_q, seed=ctx + n_q, max_blocks=ctx // 256, **W.QWEN3_4B)
+def test_cfg2_verify_and_decode(pkg, W, B, ctx, n_q, kernel_choice):
+    """The whole cfg2 grid (B x ctx, verify k=6 and decode), every sequence against the
+    float64 oracle, on both kernels; the launch plan of each point is recorded."""
+    case, want = _cfg2_case_and_oracle(W, B, ctx, n_q)
+    kind, slots, _ = pkg.attention.plan(B, n_q, 32, 8, 128, 256, ctx // 256, torch.bfloat16)
+    assert kind == ("mma" if kernel_choice == "mma" else kind)
+    out = pkg.paged_attention(case.q, case.k_cache, case.v_cache, case.block_tables, case.cache_seqlens,
+                              case.scale, n_q=n_q)
+    torch.cuda.synchronize()
+    _check(out, want, BF16_TOL)
+
+
+# one shape per decomposition of the tcgen05 plan (B200, 148 SMs): strided with 1, 2 and
+# >= 3 key chunks per (sequence, kv head), and the balanced grouped partition
+_PLAN_SHAPES = [
+    ("tcgen05_strided", 1, 16, 4096),
+    ("tcgen05_strided", 2, 8, 2048),
+    ("tcgen05_strided", 3, 5, 2048),
+    ("tcgen05_strided", 11, 1, 4096),
+    ("tcgen05_grouped", 4, 1, 512),
+    ("tcgen05_grouped", 5, 5, 4096),
+    ("tcgen05_grouped", 3, 10, 2048),
+    ("tcgen05_grouped", 2, 24, 4096),
+]
+
+
+@pytest.mark.parametrize("want_kind,want_slots,B,ctx", _PLAN_SHAPES)
+@pytest.mark.parametrize("n_q", [7, 1])
+def test_each_umma_plan_outcome(pkg, W, want_kind, want_slots, B, ctx, n_q, kernel_choice):
+    if kernel_choice == "mma":
+        pytest.skip("plan outcomes of the tcgen05 kernel")
+    if torch.cuda.get_device_properties(0).multi_processor_count != 148:
+        pytest.skip("the plan table is for 148 SMs")
+    kind, slots, _ = pkg.attention.plan(B, n_q, 32, 8, 128, 256, ctx // 256, torch.bfloat16)
+    assert (kind, slots) == (want_kind, want_slots)
+    lens = W.cfg2_lens(B, ctx, seed=7 * B + ctx)
+    lens[-1] = ctx  # the longest sequence spans every split / group boundary
+    case = W.paged_case(lens, n_q, seed=B * ctx + n_q, max_blocks=ctx // 256, **W.QWEN3_4B)
     out = pkg.paged_attention(case.q, case.k_cache, case.v_cache, case.block_tables, case.cache_seqlens,
                               case.scale, n_q=n_q)
     torch.cuda.synchronize()
@@ -163,7 +213,7 @@ def test_head_major_layout(pkg, W):
 def test_full_size_verify_rows_equal_truncated_decodes(pkg, W):
     """B=64, ctx=4096, k=6: verify row r equals a decode of length L-6+r (the causal rule)
     to within one bf16 ulp (decode and verify slice the keys of a tile differently, so
-    their fp32 summation orders differ), and a sample of sequences matches the oracle."""
+    their fp32 summation orders differ), and all 64 sequences match the oracle."""
     B, ctx, n_q = 64, 4096, 7
     case = W.paged_case([ctx] * B, n_q, seed=1, generate_on_device=True, extra_blocks=0, **W.QWEN3_4B)
     out = pkg.paged_attention(case.q, case.k_cache, case.v_cache, case.block_tables, case.cache_seqlens,
@@ -176,11 +226,7 @@ def test_full_size_verify_rows_equal_truncated_decodes(pkg, W):
                                   lens_r, case.scale, n_q=1, splits=splits)
         ver = out.view(B, n_q, 32, 128)[:, r]
         assert torch.allclose(dec.float(), ver.float(), rtol=1e-2, atol=1e-4), f"row {r}"
-    sample = [0, 17, 63]
-    sub = W.PagedCase(q=qv[sample].reshape(-1, 32, 128), k_cache=case.k_cache, v_cache=case.v_cache,
-                      block_tables=case.block_tables[sample], cache_seqlens=case.cache_seqlens[sample],
-                      scale=case.scale, n_q=n_q)
-    _check(out.view(B, n_q, 32, 128)[sample].reshape(-1, 32, 128), _oracle(sub), BF16_TOL)
+    _check(out, _oracle(case), BF16_TOL)  # every sequence against the float64 oracle
 
 
 def test_block_placement_invariance_and_determinism(pkg, W):

@@ -36,6 +36,21 @@ def test_attention_bf16_decode_and_verify_match_reference(golden, n_q):
     assert ok, err
 
 
+@pytest.mark.parametrize("name,n_q", [("attn_decode_fp32", 1), ("attn_bf16_nq1", 1), ("attn_bf16_nq4", 4)])
+def test_torch_restatement_matches_reference(golden, name, n_q):
+    """The torch restatement bench.py times as the CPU baseline reproduces the reference."""
+    import torch
+    from oracle.torch_ref import paged_attention_torch
+    g = golden(name)
+    conv = (lambda a: torch.from_numpy(bf16_bits_to_f32(a))) if "bf16" in name else torch.from_numpy
+    out = paged_attention_torch(conv(g["q"]), conv(g["k_cache"]), conv(g["v_cache"]),
+                                torch.from_numpy(g["block_tables"]), torch.from_numpy(g["cache_seqlens"]),
+                                float(g["scale"]), n_q=n_q)
+    want = g["out"] if "out" in g else g["out_f32"]
+    ok, err, _ = allclose_report(out.numpy(), want, rtol=1e-5, atol=1e-5)
+    assert ok, err
+
+
 def test_visible_keys_rule():
     # bottom-right causal: last row sees everything, row r sees L-n+r+1 keys
     assert [oatt.visible_keys(10, 4, r) for r in range(4)] == [7, 8, 9, 10]
