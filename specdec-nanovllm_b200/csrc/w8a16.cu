@@ -87,15 +87,10 @@ SDB_DEV float load_scale(const void* s, int dt, int64_t i) {
     return __half2float(reinterpret_cast<const __half*>(s)[i]);
 }
 
-// Row stride (16-bit elements) of the staged token tile: the split's k range plus 8
-// elements, so the 8 rows a warp reads at once fall on different banks.
-SDB_DEV SDB_HOST_DEV_INLINE int x_stride(int kspan) { return kspan + 8; }
-
 template <typename T, int NT, bool GROUPED>
 __global__ void __launch_bounds__(WARPS * 32) w8a16_kernel(const Params p) {
     using H = Half16<T>;
     __shared__ int last;
-    extern __shared__ __align__(16) unsigned char xs_raw[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, t = lane & 3;
     const int n0 = blockIdx.x * FEAT + warp * 16;
@@ -104,39 +99,12 @@ __global__ void __launch_bounds__(WARPS * 32) w8a16_kernel(const Params p) {
     const int nchunks = p.K / KC;
     const int c0 = sk * p.chunks_per_split;
     const int c1 = min(c0 + p.chunks_per_split, nchunks);
-    const int nc = c1 - c0;
 
     const int row0 = n0 + g, row1 = n0 + g + 8;
     const bool ok0 = row0 < p.N, ok1 = row1 < p.N;
-    const int8_t* w0 = p.w + (int64_t)(ok0 ? row0 : 0) * p.K + (int64_t)c0 * KC + t * 16;
-    const int8_t* w1 = p.w + (int64_t)(ok1 ? row1 : 0) * p.K + (int64_t)c0 * KC + t * 16;
-
-    // The weight stream starts before anything else: PF chunks of both rows in flight.
-    uint4 wa[PF], wb[PF];
-#pragma unroll
-    for (int u = 0; u < PF; ++u) {
-        if (u < nc) {
-            wa[u] = ok0 ? __ldcs(reinterpret_cast<const uint4*>(w0 + u * KC)) : make_uint4(0, 0, 0, 0);
-            wb[u] = ok1 ? __ldcs(reinterpret_cast<const uint4*>(w1 + u * KC)) : make_uint4(0, 0, 0, 0);
-        }
-    }
-
-    // The split's token tile (8 * NT rows x its k range) is staged in shared memory once;
-    // rows past M are zeros.
-    const int kspan = nc * KC, xst = x_stride(kspan);
-    T* xs = reinterpret_cast<T*>(xs_raw);
-    {
-        const T* xb = reinterpret_cast<const T*>(p.x);
-        const int vec_per_row = kspan / 8;
-        for (int i = threadIdx.x; i < 8 * NT * vec_per_row; i += WARPS * 32) {
-            const int r = i / vec_per_row, v = i % vec_per_row;
-            const int m = m0 + r;
-            uint4 val = make_uint4(0, 0, 0, 0);
-            if (m < p.M) val = __ldg(reinterpret_cast<const uint4*>(xb + (int64_t)m * p.x_srow + c0 * KC + v * 8));
-            *reinterpret_cast<uint4*>(xs + r * xst + v * 8) = val;
-        }
-    }
-    __syncthreads();
+    const int8_t* w0 = p.w + (int64_t)(ok0 ? row0 : 0) * p.K + t * 16;
+    const int8_t* w1 = p.w + (int64_t)(ok1 ? row1 : 0) * p.K + t * 16;
+    const T* xb = reinterpret_cast<const T*>(p.x);
 
     float acc[NT][4];
     float gacc[GROUPED ? NT : 1][4];
@@ -148,20 +116,23 @@ __global__ void __launch_bounds__(WARPS * 32) w8a16_kernel(const Params p) {
     }
     const int gchunks = GROUPED ? p.group / KC : 1;
 
-    // Rolling prefetch: chunk i is consumed from slot i % PF, which is refilled at once
-    // with chunk i + PF, so PF chunks stay in flight while the warp computes.
-    for (int base = 0; base < nc; base += PF) {
+    for (int cb = c0; cb < c1; cb += UNROLL) {
+        uint4 wa[UNROLL], wb[UNROLL];
 #pragma unroll
-        for (int u = 0; u < PF; ++u) {
-            const int i = base + u;
-            if (i >= nc) break;
+        for (int u = 0; u < UNROLL; ++u) {
+            const int c = cb + u;
+            if (c < c1) {
+                wa[u] = ok0 ? __ldcs(reinterpret_cast<const uint4*>(w0 + c * KC)) : make_uint4(0, 0, 0, 0);
+                wb[u] = ok1 ? __ldcs(reinterpret_cast<const uint4*>(w1 + c * KC)) : make_uint4(0, 0, 0, 0);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < UNROLL; ++u) {
+            const int c = cb + u;
+            if (c >= c1) break;
             uint32_t a[4][4];
             const uint32_t wa32[4] = {wa[u].x, wa[u].y, wa[u].z, wa[u].w};
             const uint32_t wb32[4] = {wb[u].x, wb[u].y, wb[u].z, wb[u].w};
-            if (i + PF < nc) {
-                wa[u] = ok0 ? __ldcs(reinterpret_cast<const uint4*>(w0 + (i + PF) * KC)) : make_uint4(0, 0, 0, 0);
-                wb[u] = ok1 ? __ldcs(reinterpret_cast<const uint4*>(w1 + (i + PF) * KC)) : make_uint4(0, 0, 0, 0);
-            }
 #pragma unroll
             for (int s = 0; s < 4; ++s) {
                 i8x4_to_pairs<T>(wa32[s], a[s][0], a[s][2]);
@@ -169,14 +140,18 @@ __global__ void __launch_bounds__(WARPS * 32) w8a16_kernel(const Params p) {
             }
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
-                const uint4* xp = reinterpret_cast<const uint4*>(xs + (nt * 8 + g) * xst + i * KC + t * 16);
-                const uint4 x0 = xp[0], x1 = xp[1];
+                const int m = m0 + nt * 8 + g;
+                uint4 x0 = make_uint4(0, 0, 0, 0), x1 = make_uint4(0, 0, 0, 0);
+                if (m < p.M) {
+                    const uint4* xp = reinterpret_cast<const uint4*>(xb + (int64_t)m * p.x_srow + c * KC + t * 16);
+                    x0 = __ldg(xp);
+                    x1 = __ldg(xp + 1);
+                }
                 const uint32_t xw[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
                 float* dst = GROUPED ? gacc[GROUPED ? nt : 0] : acc[nt];
 #pragma unroll
                 for (int s = 0; s < 4; ++s) H::mma(dst, a[s], xw[2 * s], xw[2 * s + 1]);
             }
-            const int c = c0 + i;
             if (GROUPED && (((c + 1) % gchunks) == 0 || c + 1 == c1)) {
                 const int grp = c / gchunks;
                 const int ng = p.K / p.group;
