@@ -446,6 +446,109 @@ def run_ours(args):
     return 0
 
 
+# --------------------------------------------------------------------------- tensor-parallel step
+def run_tp_step(args):
+    """One tensor-parallel verify step of the target's attention block on N GPUs: every
+    rank holds 32/N q and 8/N kv heads of the B=64 x 4096 k=6 verify batch, runs the paged
+    verify attention over its heads, then its slice of the W8A16 o_proj (row-parallel,
+    4096/N input columns -> 2560) and the NCCL all-reduce of the (448, 2560) bf16 partial
+    sums (RowParallelLinear, linear.py:165-170).  Times G steps per captured graph, max
+    over ranks, plus each part alone."""
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    pkg = load_package()
+    from specdec_nanovllm_b200 import workloads
+    from specdec_nanovllm_b200.partition import RowParallelInt8Linear, tp_head_shard
+    B = args.global_batch
+    hs = tp_head_shard(HQ, HKV, world, rank)
+    case = workloads.paged_case([CTX] * B, N_Q, Hq=hs.num_q_heads, Hkv=hs.num_kv_heads, D=D, page=PAGE,
+                                dtype=torch.bfloat16, device=dev, seed=2000 + rank, extra_blocks=0,
+                                generate_on_device=True)
+    T = B * N_Q
+    K_o, N_o = workloads.W8A16_SHAPES["o"]
+    g = torch.Generator(device=dev).manual_seed(7)
+    qw = torch.randint(-127, 128, (N_o, K_o), generator=g, device=dev, dtype=torch.int32).to(torch.int8)
+    sc = (torch.randn(N_o, generator=g, device=dev).abs() * 0.01).to(torch.bfloat16)
+    oproj = RowParallelInt8Linear(qw, sc, None, rank, world)
+    attn_out = torch.empty_like(case.q)
+
+    def attention():
+        pkg.paged_attention(case.q, case.k_cache, case.v_cache, case.block_tables, case.cache_seqlens,
+                            case.scale, n_q=N_Q, out=attn_out)
+
+    y = torch.empty(T, N_o, dtype=torch.bfloat16, device=dev)
+
+    def matmul():
+        pkg.int8_linear(attn_out.view(T, -1), oproj.qweight, oproj.scale, out=y)
+
+    def allreduce():
+        if world > 1:
+            dist.all_reduce(y)
+
+    def step():
+        attention()
+        matmul()
+        allreduce()
+
+    def time_graph(fn, G=20, reps=50):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        st = torch.cuda.Stream(dev)
+        st.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(st):
+            with torch.cuda.graph(gr, stream=st):
+                for _ in range(G):
+                    fn()
+        torch.cuda.current_stream().wait_stream(st)
+        gr.replay()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            gr.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1e3 / (G * reps)
+        del gr
+        if world > 1:
+            t = torch.tensor([us], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            us = float(t.item())
+        return us
+
+    step()
+    parts = {"attention": time_graph(attention), "o_proj_int8": time_graph(matmul)}
+    parts["all_reduce"] = time_graph(allreduce) if world > 1 else 0.0
+    total = time_graph(step)
+    ar_bytes = T * N_o * 2
+    if rank == 0:
+        line = {"metric": "tensor-parallel verify attention block us/step", "value": round(total, 2), "unit": "us",
+                "n_gpus": world, "higher_is_better": False, "dtype": "bf16", "data": "synthetic",
+                "config": {"workload": f"verify attention B={B} ctx={CTX} k={K_SPEC}, heads {hs.num_q_heads}/"
+                                       f"{hs.num_kv_heads} per rank, o_proj int8 {K_o // world}->{N_o} per rank, "
+                                       f"all-reduce of ({T}, {N_o}) bf16", "parallelism": f"tp{world}"},
+                "parts_us": {k: round(v, 2) for k, v in parts.items()},
+                "all_reduce_bytes": ar_bytes,
+                "all_reduce_busbw_gbs": round(2 * (world - 1) / world * ar_bytes / (parts["all_reduce"] * 1e-6) / 1e9, 1)
+                if world > 1 else None}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    return 0
+
+
 # --------------------------------------------------------------------------- side modes
 def _time_events(fn, steps, warmup, per_graph=20):
     """Device ms per call: ``per_graph`` calls captured in one CUDA graph, replayed so that
@@ -638,7 +741,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--skip-cpu", action="store_true", help="omit the CPU baseline leg")
-    ap.add_argument("--mode", choices=["verify_attn", "decode_attn", "attn_sweep", "verify_batch", "w8a16", "sample"],
+    ap.add_argument("--mode", choices=["verify_attn", "decode_attn", "attn_sweep", "verify_batch", "w8a16", "sample", "tp_step"],
                     default="verify_attn", help="verify_attn is the headline; the others measure the "
                     "secondary kernels of the path on one GPU")
     ap.add_argument("--m", type=int, default=1, help="tokens (M) for --mode w8a16")
@@ -646,6 +749,8 @@ def main():
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":
         return run_reference(args)
+    if args.mode == "tp_step":
+        return run_tp_step(args)
     if args.mode != "verify_attn":
         return run_side(args)
     return run_ours(args)
