@@ -549,6 +549,93 @@ def run_tp_step(args):
     return 0
 
 
+# --------------------------------------------------------------------------- end-to-end step
+def run_specdec_e2e(args):
+    """a speculative decode step with a random-init Qwen3-4B
+    target and Qwen3-0.6B draft (bf16), k = 6, 64 sequences at 2048 tokens of context in
+    paged KV caches, CUDA graphs; sequences sharded over the ranks under torchrun.
+    Tokens per step = accepted drafts + the bonus token of every sequence."""
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
+    load_package()
+    from specdec_nanovllm_b200.partition import shard_range
+    from specdec_nanovllm_b200.specdec import QWEN3_06B, QWEN3_4B, RandomQwen3, SpecDecodeStep
+    Bg, ctx, k = args.global_batch, 2048, K_SPEC
+    lo, hi = shard_range(Bg, world, rank)
+    target = RandomQwen3(QWEN3_4B, dev, seed=1)
+    draft = RandomQwen3(QWEN3_06B, dev, seed=2)
+    st = SpecDecodeStep(target, draft, hi - lo, ctx, k, dev, seed=100 + lo)
+    st.prepare()
+    steps = max(1, min(args.steps, 50))
+    acc_h = torch.empty(steps, hi - lo, dtype=torch.int64, pin_memory=True)
+    for _ in range(args.warmup):
+        st.step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier(device_ids=[local])
+    sampler = ClockSampler(dev.index)
+    sampler.start()
+    time.sleep(0.3)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(steps):
+        r = st.step()
+        acc_h[i].copy_(r.accepted, non_blocking=True)   # the engine reads the counts back every step
+    e1.record()
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    ms = e0.elapsed_time(e1) / steps
+    tokens = float((acc_h + 1).sum()) / steps                # accepted drafts + bonus, this rank
+    # phases, timed apart (same graphs)
+    def phase(fn, n=10):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(n):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / n
+    t_draft = phase(st.g_draft.replay)
+    t_target = phase(st.g_target.replay)
+    from specdec_nanovllm_b200 import verify_batch
+    t_verify = phase(lambda: verify_batch(st.draft_logits, st.target_logits, st.cands, st.temps.view(-1),
+                                          seed=7, offset=0))
+    stats = torch.tensor([ms, tokens, t_draft, t_target, t_verify], device=dev, dtype=torch.float64)
+    if world > 1:
+        mx = stats.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        sm = stats.clone()
+        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+        ms, t_draft, t_target, t_verify = float(mx[0]), float(mx[2]), float(mx[3]), float(mx[4])
+        tokens = float(sm[1])
+    tok_s = tokens / (ms * 1e-3)
+    if rank == 0:
+        line = {"metric": "spec-decode tok/s, Qwen3-4B target + Qwen3-0.6B draft, k=6", "value": round(tok_s, 1),
+                "unit": "tok/s", "n_gpus": world, "steps": steps, "warmup": args.warmup,
+                "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                "dtype": "bf16", "data": "synthetic (random-init weights, N(0,1) KV context)",
+                "config": {"workload": f"spec decode step, {Bg} sequences x {ctx} context, k={k}, CUDA graphs",
+                           "global_batch": Bg, "seq_len": ctx, "k": k, "parallelism": f"seq-shard{world}"},
+                "tokens_per_step": round(tokens, 2),
+                "mean_accepted_per_seq": round(tokens / Bg - 1.0, 3),
+                "phases_ms": {"draft_k_steps": round(t_draft, 3), "target_verify_forward": round(t_target, 3),
+                              "verify_batch": round(t_verify, 3)},
+                "clocks": clocks}
+        print(json.dumps(line), flush=True)
+    st.close()
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    return 0
+
+
 # --------------------------------------------------------------------------- side modes
 def _time_events(fn, steps, warmup, per_graph=20):
     """Device ms per call: ``per_graph`` calls captured in one CUDA graph, replayed so that
@@ -741,7 +828,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--skip-cpu", action="store_true", help="omit the CPU baseline leg")
-    ap.add_argument("--mode", choices=["verify_attn", "decode_attn", "attn_sweep", "verify_batch", "w8a16", "sample", "tp_step"],
+    ap.add_argument("--mode", choices=["verify_attn", "decode_attn", "attn_sweep", "verify_batch", "w8a16", "sample", "tp_step",
+                             "specdec_e2e"],
                     default="verify_attn", help="verify_attn is the headline; the others measure the "
                     "secondary kernels of the path on one GPU")
     ap.add_argument("--m", type=int, default=1, help="tokens (M) for --mode w8a16")
@@ -751,6 +839,8 @@ def main():
         return run_reference(args)
     if args.mode == "tp_step":
         return run_tp_step(args)
+    if args.mode == "specdec_e2e":
+        return run_specdec_e2e(args)
     if args.mode != "verify_attn":
         return run_side(args)
     return run_ours(args)

@@ -1,0 +1,231 @@
+"""End-to-end speculative decode step on the sm_100a kernels, with random-init Qwen3 models.
+
+The reference's step (``nanovllm/engine/model_runner.py:945-1120`` with the batched draft
+of ``nanovllm/spec_decode/draft_proposer.py:414-518``):
+
+1. propose: k batched draft decode steps.  Step s feeds the last confirmed token (s = 0)
+   or draft token s-1 at position len-1+s, writes its K/V into the draft's paged cache,
+   and samples draft token s from softmax(logits / T) with exponential noise, keeping
+   the raw logits (:495-510);
+2. verify: one target forward over the k+1 tokens of every sequence (positions
+   len-1 .. len+k-1, causal inside the window; ``prepare_verify``, :492-584), its K/V
+   written into the target cache, then the LM head;
+3. ``verify_batch`` on the raw draft logits and the target logits: accepted prefix
+   length and the bonus token of every sequence (:1051-1119, batched here).
+
+Every layer runs the sm_100a kernels of this package -- the fused split / q-k RMSNorm /
+rotary / KV store (``qk_norm_rope_store``), the paged decode or verify attention, the
+draft sampler and ``verify_batch`` -- around bf16 cuBLAS GEMMs for the projections and
+the LM head (``torch.nn.functional.linear``, the reference's ``F.linear``) and torch for
+the embedding, the residual RMSNorms and SiLU * up (``layers/layernorm.py``,
+``layers/activation.py``).  The draft's k steps are one captured CUDA graph and so is
+the target's verify forward (the reference captures both, ``model_runner.py:1218-1347``).
+The draft noise inside the graph comes from torch's generator, which advances on every
+replay; ``verify_batch`` runs after the graph with a fresh Philox offset per step.
+
+Models are random-init (there are no checkpoints): weights N(0, 0.02) in bf16, norm
+weights 1, tied embeddings.  The KV caches start filled with N(0, 1) values standing for
+a ``context``-token prefix, so a step runs at that context without a prefill.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.nn.functional as F
+
+from .attention import paged_attention
+from .prologue import qk_norm_rope_store, rope_cos_sin_cache
+from .sampler import draft_sample_step
+from .verify import verify_batch
+
+
+@dataclass(frozen=True)
+class Qwen3Shape:
+    layers: int
+    hidden: int
+    heads: int
+    kv_heads: int
+    ffn: int
+    vocab: int = 151936
+    head_dim: int = 128
+    eps: float = 1e-6
+    rope_theta: float = 1e6
+
+
+QWEN3_4B = Qwen3Shape(layers=36, hidden=2560, heads=32, kv_heads=8, ffn=9728)
+QWEN3_06B = Qwen3Shape(layers=28, hidden=1024, heads=16, kv_heads=8, ffn=3072)
+
+
+def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float, residual: torch.Tensor | None = None):
+    """``RMSNorm.rms_forward`` / ``add_rms_forward`` (layers/layernorm.py:17-43): float32
+    statistics, the normalised value rounded to the model dtype before the weight."""
+    if residual is not None:
+        xf = x.float() + residual.float()
+        residual = xf.to(x.dtype)
+    else:
+        xf = x.float()
+        residual = x
+    y = xf * torch.rsqrt(xf.pow(2).mean(dim=-1, keepdim=True) + eps)
+    return y.to(x.dtype) * w, residual
+
+
+class RandomQwen3:
+    """A Qwen3 decoder with random bf16 weights, run on the package's kernels."""
+
+    def __init__(self, shape: Qwen3Shape, device, seed: int, max_position: int = 8192,
+                 dtype=torch.bfloat16):
+        self.s = shape
+        self.dtype = dtype
+        g = torch.Generator(device=device).manual_seed(seed)
+        H, D = shape.hidden, shape.head_dim
+
+        def w(out_f, in_f):
+            return (torch.randn(out_f, in_f, generator=g, device=device, dtype=torch.float32) * 0.02).to(dtype)
+
+        self.embed = w(shape.vocab, H)          # tied with the LM head
+        self.layers = []
+        for _ in range(shape.layers):
+            self.layers.append(dict(
+                ln1=torch.ones(H, device=device, dtype=dtype),
+                ln2=torch.ones(H, device=device, dtype=dtype),
+                qkv=w((shape.heads + 2 * shape.kv_heads) * D, H),
+                q_norm=torch.ones(D, device=device, dtype=dtype),
+                k_norm=torch.ones(D, device=device, dtype=dtype),
+                o=w(H, shape.heads * D),
+                gate_up=w(2 * shape.ffn, H),
+                down=w(H, shape.ffn)))
+        self.norm = torch.ones(H, device=device, dtype=dtype)
+        self.cos_sin = rope_cos_sin_cache(D, max_position, shape.rope_theta, device=device)
+        self.scale = 1.0 / math.sqrt(D)
+
+    def new_cache(self, num_blocks: int, page: int, device, seed: int):
+        """Per layer (num_blocks, page, Hkv, D) K and V caches, filled with N(0, 1)."""
+        g = torch.Generator(device=device).manual_seed(seed)
+        shp = (num_blocks, page, self.s.kv_heads, self.s.head_dim)
+        return [(torch.randn(shp, generator=g, device=device, dtype=self.dtype),
+                 torch.randn(shp, generator=g, device=device, dtype=self.dtype)) for _ in range(self.s.layers)]
+
+    def forward(self, ids, positions, slots, block_tables, seqlens, n_q: int, cache) -> torch.Tensor:
+        """Hidden states (T, H) of T = B * n_q tokens, rows b * n_q .. b * n_q + n_q - 1 of
+        sequence b at consecutive positions ending at seqlens[b] - 1 (decode: n_q = 1)."""
+        s = self.s
+        h = F.embedding(ids, self.embed)
+        residual = None
+        for lw, (kc, vc) in zip(self.layers, cache):
+            x, residual = rms_norm(h, lw["ln1"], s.eps, residual)
+            qkv = F.linear(x, lw["qkv"])
+            q = qk_norm_rope_store(qkv, positions, s.heads, s.kv_heads, s.head_dim, self.cos_sin,
+                                   lw["q_norm"], lw["k_norm"], s.eps, k_cache=kc, v_cache=vc,
+                                   slot_mapping=slots)
+            o = paged_attention(q, kc, vc, block_tables, seqlens, self.scale, n_q=n_q)
+            h = F.linear(o.view(o.shape[0], -1), lw["o"])
+            x, residual = rms_norm(h, lw["ln2"], s.eps, residual)
+            gu = F.linear(x, lw["gate_up"])
+            h = F.linear(F.silu(gu[:, :s.ffn]) * gu[:, s.ffn:], lw["down"])
+        h, _ = rms_norm(h, self.norm, s.eps, residual)
+        return h
+
+    def logits(self, h: torch.Tensor) -> torch.Tensor:
+        return F.linear(h, self.embed)
+
+
+class SpecDecodeStep:
+    """B sequences at a fixed ``context`` (tokens already in both caches), k drafts per
+    step.  ``step()`` runs propose -> verify -> verify_batch and returns the accepted
+    counts and bonus tokens (device tensors); the caches keep the context fixed, so every
+    step measures the same work.  Sequences own disjoint blocks (one pool per model,
+    scattered block ids)."""
+
+    def __init__(self, target: RandomQwen3, draft: RandomQwen3, B: int, context: int, k: int, device,
+                 page: int = 256, seed: int = 0, use_graphs: bool = True):
+        self.t, self.d, self.B, self.L, self.k = target, draft, B, context, k
+        self.dev = device
+        self.page = page
+        max_len = context + k + 1
+        nblk = (max_len + page - 1) // page
+        gen = torch.Generator().manual_seed(seed)
+        perm = torch.randperm(B * nblk, generator=gen).to(torch.int32)
+        self.block_tables = perm.view(B, nblk).to(device)
+        self.t_cache = target.new_cache(B * nblk, page, device, seed + 1)
+        self.d_cache = draft.new_cache(B * nblk, page, device, seed + 2)
+        self.last_tokens = torch.randint(0, target.s.vocab, (B,), generator=gen).to(device)
+        self.temps = torch.ones(B, 1, device=device)
+        bt = self.block_tables.long()
+        base = torch.full((B,), context - 1, dtype=torch.int64, device=device)  # last confirmed token
+
+        def slots_at(pos):                                                  # (B, n) positions -> slots
+            return (bt.gather(1, pos // page) * page + pos % page).to(torch.int32)
+
+        # draft step s: one token per sequence at position L-1+s, cache length L+s
+        self.d_pos = [(base + s).view(B) for s in range(k)]
+        self.d_slots = [slots_at((base + s).view(B, 1)).view(B) for s in range(k)]
+        self.d_lens = [torch.full((B,), context + s, dtype=torch.int32, device=device) for s in range(k)]
+        # verify: k+1 tokens per sequence at L-1 .. L+k-1, cache length L+k
+        vpos = base.view(B, 1) + torch.arange(k + 1, device=device).view(1, k + 1)
+        self.v_pos = vpos.reshape(-1)
+        self.v_slots = slots_at(vpos).reshape(-1)
+        self.v_lens = torch.full((B,), context + k, dtype=torch.int32, device=device)
+        V = target.s.vocab
+        self.draft_logits = torch.empty(B, k, V, device=device)
+        self.cands = torch.empty(B, k, dtype=torch.int64, device=device)
+        self.v_ids = torch.empty(B, k + 1, dtype=torch.int64, device=device)
+        self.target_logits = None
+        self.noise = torch.empty(B, V, device=device)
+        self.n_steps = 0
+        self.use_graphs = use_graphs
+        self.g_draft = self.g_target = None
+
+    # ---- the two phases (captured as graphs after one eager run)
+    def _propose(self):
+        tok = self.last_tokens
+        for s in range(self.k):
+            h = self.d.forward(tok, self.d_pos[s], self.d_slots[s], self.block_tables, self.d_lens[s], 1,
+                               self.d_cache)
+            lg = self.d.logits(h)
+            self.noise.exponential_(1.0)
+            tok = draft_sample_step(lg, self.temps, self.draft_logits, self.cands, s, exponentials=self.noise)
+
+    def _verify_forward(self):
+        self.v_ids[:, 0] = self.last_tokens
+        self.v_ids[:, 1:] = self.cands
+        h = self.t.forward(self.v_ids.view(-1), self.v_pos, self.v_slots, self.block_tables, self.v_lens,
+                           self.k + 1, self.t_cache)
+        self.target_logits = self.t.logits(h).view(self.B, self.k + 1, -1)
+
+    def _capture(self, fn):
+        g = torch.cuda.CUDAGraph()
+        st = torch.cuda.Stream(self.dev)
+        st.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(st):
+            with torch.cuda.graph(g, stream=st):
+                fn()
+        torch.cuda.current_stream().wait_stream(st)
+        return g
+
+    def prepare(self):
+        """One eager step (sizes every workspace), then the graph captures."""
+        self._propose()
+        self._verify_forward()
+        torch.cuda.synchronize()
+        if self.use_graphs:
+            self.g_draft = self._capture(self._propose)
+            self.g_target = self._capture(self._verify_forward)
+            self.graph_target_logits = self.target_logits  # the graph's output buffer
+
+    def step(self):
+        if self.use_graphs:
+            self.g_draft.replay()
+            self.g_target.replay()
+            self.target_logits = self.graph_target_logits
+        else:
+            self._propose()
+            self._verify_forward()
+        self.n_steps += 1
+        return verify_batch(self.draft_logits, self.target_logits, self.cands, self.temps.view(-1),
+                            seed=1234, offset=self.n_steps)
+
+    def close(self):
+        self.g_draft = self.g_target = None
