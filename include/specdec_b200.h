@@ -393,6 +393,27 @@ int sdb_w8a16_linear(const void* x, int64_t x_stride_row, const int8_t* qweight,
 int sdb_quantize_weight(const void* w, int w_dtype, int8_t* q, void* scale, int scale_dtype,
                         int N, int K, int group_size, void* stream);
 
+/* =========================================================================
+ * Decoder-layer elementwise steps (model side of the end-to-end step).
+ *
+ * sdb_rms_norm replaces RMSNorm.rms_forward / add_rms_forward
+ *                                           nanovllm/layers/layernorm.py:17-43
+ *   s = x (+ residual_in) in float32; residual_out (may be NULL) = s rounded to dtype;
+ *   out = (s * rsqrt(mean(s^2) + eps)) rounded to dtype, times weight, rounded.
+ *   x, residual_in, out, residual_out (T, H) rows *_stride elements apart (16-byte aligned
+ *   rows; out may alias x and residual_out residual_in), weight (H); H % 8 == 0, H <= 8192.
+ * sdb_silu_mul replaces SiluAndMul.forward  nanovllm/layers/activation.py:8-13
+ *   gate_up (T, 2F) rows [gate | up], out (T, F) = silu(gate) * up, silu rounded to dtype
+ *   before the product as torch rounds it; F % 8 == 0.
+ * dtype: SDB_BF16 or SDB_F16.
+ * ========================================================================= */
+int sdb_rms_norm(const void* x, int64_t x_stride, const void* residual_in, int64_t residual_in_stride,
+                 void* out, int64_t out_stride, void* residual_out, int64_t residual_out_stride,
+                 const void* weight, int T, int H, float eps, int dtype, void* stream);
+
+int sdb_silu_mul(const void* gate_up, int64_t gate_up_stride, void* out, int64_t out_stride,
+                 int T, int F, int dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

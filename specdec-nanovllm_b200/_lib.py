@@ -103,6 +103,9 @@ SIGNATURES = {
         _c_p, _c_i64, _c_p, _c_p, _c_i32, _c_i32, _c_p, _c_p, _c_i64, _c_i32, _c_i32, _c_i32,
         _c_i32, _c_p, _c_sz, _c_p]),
     "sdb_quantize_weight": (_c_i32, [_c_p, _c_i32, _c_p, _c_p, _c_i32, _c_i32, _c_i32, _c_i32, _c_p]),
+    "sdb_rms_norm": (_c_i32, [_c_p, _c_i64, _c_p, _c_i64, _c_p, _c_i64, _c_p, _c_i64, _c_p,
+                              _c_i32, _c_i32, _c_f32, _c_i32, _c_p]),
+    "sdb_silu_mul": (_c_i32, [_c_p, _c_i64, _c_p, _c_i64, _c_i32, _c_i32, _c_i32, _c_p]),
 }
 
 _lib = None

@@ -15,10 +15,10 @@ of ``nanovllm/spec_decode/draft_proposer.py:414-518``):
 
 Every layer runs the sm_100a kernels of this package -- the fused split / q-k RMSNorm /
 rotary / KV store (``qk_norm_rope_store``), the paged decode or verify attention, the
-draft sampler and ``verify_batch`` -- around bf16 cuBLAS GEMMs for the projections and
-the LM head (``torch.nn.functional.linear``, the reference's ``F.linear``) and torch for
-the embedding, the residual RMSNorms and SiLU * up (``layers/layernorm.py``,
-``layers/activation.py``).  The draft's k steps are one captured CUDA graph and so is
+draft sampler and ``verify_batch`` -- and the residual RMSNorm and SiLU * up of ``layers.py``
+(``layers/layernorm.py``, ``layers/activation.py``) -- around bf16 cuBLAS GEMMs for the
+projections and the LM head (``torch.nn.functional.linear``, the reference's
+``F.linear``) and torch's embedding lookup.  The draft's k steps are one captured CUDA graph and so is
 the target's verify forward (the reference captures both, ``model_runner.py:1218-1347``).
 The draft noise inside the graph comes from torch's generator, which advances on every
 replay; ``verify_batch`` runs after the graph with a fresh Philox offset per step.
@@ -37,6 +37,8 @@ import torch
 import torch.nn.functional as F
 
 from .attention import paged_attention
+from .layers import rms_norm as layer_rms_norm
+from .layers import silu_and_mul
 from .prologue import qk_norm_rope_store, rope_cos_sin_cache
 from .sampler import draft_sample_step
 from .verify import verify_batch
@@ -60,16 +62,11 @@ QWEN3_06B = Qwen3Shape(layers=28, hidden=1024, heads=16, kv_heads=8, ffn=3072)
 
 
 def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float, residual: torch.Tensor | None = None):
-    """``RMSNorm.rms_forward`` / ``add_rms_forward`` (layers/layernorm.py:17-43): float32
-    statistics, the normalised value rounded to the model dtype before the weight."""
-    if residual is not None:
-        xf = x.float() + residual.float()
-        residual = xf.to(x.dtype)
-    else:
-        xf = x.float()
-        residual = x
-    y = xf * torch.rsqrt(xf.pow(2).mean(dim=-1, keepdim=True) + eps)
-    return y.to(x.dtype) * w, residual
+    """``RMSNorm`` with the residual convention of ``Qwen3DecoderLayer.forward``
+    (qwen3.py:145-159): without a residual the input itself becomes the residual."""
+    if residual is None:
+        return layer_rms_norm(x, w, eps), x
+    return layer_rms_norm(x, w, eps, residual=residual)
 
 
 class RandomQwen3:
@@ -124,7 +121,7 @@ class RandomQwen3:
             h = F.linear(o.view(o.shape[0], -1), lw["o"])
             x, residual = rms_norm(h, lw["ln2"], s.eps, residual)
             gu = F.linear(x, lw["gate_up"])
-            h = F.linear(F.silu(gu[:, :s.ffn]) * gu[:, s.ffn:], lw["down"])
+            h = F.linear(silu_and_mul(gu), lw["down"])
         h, _ = rms_norm(h, self.norm, s.eps, residual)
         return h
 
