@@ -47,6 +47,10 @@ constexpr int BS_CONSUMERS = SUB;          // warps, 512 logits of each chunk ap
 constexpr int BS_EPT = CHUNK1 / (32 * BS_CONSUMERS);
 constexpr int BS_THREADS = 32 * (BS_CONSUMERS + 1);
 constexpr int BS_SMEM = BS_STAGES * CHUNK1 * 4;
+// fused residual + bonus pass: candidate columns kept per chunk, and the columns whose
+// upper bound reaches the chunk's lower bound that get an exact evaluation
+constexpr int RB_CAP = 8;
+constexpr int RB_LIVE = 64;
 
 struct Params {
     const void* draft;     // (B, k, V)
@@ -66,6 +70,8 @@ struct Params {
     float2* stats;         // [rows][C1 * SUB]  (max, sumexp) per chunk and warp
     float2* rsum;          // [B][C2]     (sum resid, sum p[a])
     float2* amax;          // [B][C2]     (value, index as float bits)
+    int* ncand;            // [B][C2]     fused residual + bonus pass: candidates kept, RB_CAP + 1 = all
+    int* cand;             // [B][C2][RB_CAP] their columns
     int* counters;         // [B], zero between calls
     struct Decision* dec;  // [B]
     int* err;
@@ -904,8 +910,243 @@ __global__ void __launch_bounds__(THREADS) vs_bonus(const Params p) {
     }
 }
 
+// ------------------------------------------------------------------ passes 3 + 4 fused
+// One read of row a (single device, vector form).  Per chunk: the residual and p sums in
+// the order of vs_resid_sums (so the normaliser Z is the same float), and the columns
+// that can hold the chunk's bonus argmax without knowing Z.  With exact v (the residual)
+// and exact E the bonus value is x = fl(fl(v / Z) / E), i.e. y = v / E times the positive
+// constant 1 / Z up to a relative 2^-23; so a column with fl(v / E) below the chunk's
+// best by more than the band 2^-20 cannot be the argmax, and the kept columns (normally
+// one) are re-evaluated exactly once Z is known.  E comes from the Philox word alone as
+// bounds (as in vs_bonus), exactly only for columns whose bound reaches the chunk's
+// lower bound.  A chunk whose residuals are all zero keeps its first column (every x
+// there is 0); a chunk with more than RB_CAP candidates or RB_LIVE live columns, and the
+// p fallback (zero residual mass, verify.py:151), are evaluated in full by the last CTA
+// of the sequence, which writes the bonus token.
+__global__ void __launch_bounds__(THREADS) vs_resid_bonus(const Params p) {
+    __shared__ float sh[THREADS / 32];
+    __shared__ int nlive, nkeep, last;
+    __shared__ int live_col[RB_LIVE];
+    __shared__ float live_y[RB_LIVE];
+    __shared__ float zsh;
+    __shared__ int use_p, any_ovf;
+    __shared__ float bv[THREADS / 32];
+    __shared__ int bi[THREADS / 32];
+    const int b = blockIdx.x, c = blockIdx.y;
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    if (threadIdx.x == 0) {
+        nlive = 0;
+        nkeep = 0;
+        any_ovf = 0;
+    }
+    const Decision d = load_decision(p, b);
+    const float T = p.temps ? p.temps[b] : 1.0f;
+    const Row tr = target_row_a(p, b, d);
+    const Row dr = draft_row_a(p, b, d);
+    const int base = c * CHUNK2;
+    const int n = min(CHUNK2, p.V - base);
+    float4 xt[EPT2 / 4], xd[EPT2 / 4];
+#pragma unroll
+    for (int q = 0; q < EPT2 / 4; ++q) {
+        xt[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+        xd[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int q2 = 0; q2 < EPT2 / 8; ++q2) {
+        const int idx = group_col(2 * q2);
+        if (idx < n) {
+            tr.at8(base + idx, n - idx, xt[2 * q2], xt[2 * q2 + 1]);
+            if (dr.p) dr.at8(base + idx, n - idx, xd[2 * q2], xd[2 * q2 + 1]);
+        }
+    }
+    float sr = 0.f, sp = 0.f;
+    float rv[EPT2], yhi[EPT2];
+    float lbmax = 0.f;
+    auto sweep = [&](auto unit) {
+#pragma unroll
+        for (int q = 0; q < EPT2 / 4; ++q) {
+            const int idx = group_col(q);
+            const bool in = idx < n;
+            const float t4[4] = {xt[q].x, xt[q].y, xt[q].z, xt[q].w};
+            const float d4[4] = {xd[q].x, xd[q].y, xd[q].z, xd[q].w};
+            uint32_t w4[4] = {(uint32_t)(base + idx) >> 2, (uint32_t)b, 1u, p.offset};
+            if (!p.e && in) philox(w4, p.seed_lo, p.seed_hi);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const int j = 4 * q + e;
+                float r = 0.f, pv = 0.f;
+                if (in) {
+                    resid_of<decltype(unit)::value>(p, d, T, t4[e], d4[e], r, pv);
+                    sr += r;
+                    sp += pv;
+                }
+                float Elo, Ehi;
+                if (p.e) {
+                    Elo = Ehi = in ? fmaxf(p.e[(int64_t)b * p.Vg + base + idx + e], 1e-10f) : 1.f;
+                } else {
+                    // -log U in [1 - U, (1 - U)(3 - 2U)] for U >= 1/2 and <= 17 always (see vs_bonus)
+                    const float U = word_to_open_uniform(w4[e]);
+                    Elo = fmaxf((1.0f - U) * 0.99999f, 1e-10f);
+                    Ehi = U >= 0.5f ? fmaxf((1.0f - U) * (3.0f - 2.0f * U) * 1.00002f, 1e-10f) : 17.0f;
+                }
+                rv[j] = in ? r : -1.f;
+                yhi[j] = in ? __fdividef(r, Elo) * 1.0001f : -1.f;
+                if (in) lbmax = fmaxf(lbmax, __fdividef(r, Ehi) * 0.9999f);
+            }
+        }
+    };
+    if (T == 1.0f) sweep(std::true_type{});
+    else sweep(std::false_type{});
+    // chunk sums, reduced as vs_resid_sums reduces them
+    const float csr = block_reduce(sr, [](float a, float b2) { return a + b2; }, sh);
+    const float csp = block_reduce(sp, [](float a, float b2) { return a + b2; }, sh);
+    const float LB = block_reduce(lbmax, [](float a, float b2) { return fmaxf(a, b2); }, sh);
+    float ymax_hi = -1.f;
+#pragma unroll
+    for (int j = 0; j < EPT2; ++j) ymax_hi = fmaxf(ymax_hi, yhi[j]);
+    const float YH = block_reduce(ymax_hi, [](float a, float b2) { return fmaxf(a, b2); }, sh);
+    float rpos = 0.f;
+#pragma unroll
+    for (int j = 0; j < EPT2; ++j) rpos = fmaxf(rpos, rv[j]);
+    // a positive residual whose bounds underflowed to 0: evaluate the chunk in full
+    bool overflow = YH <= 0.f && block_reduce(rpos, [](float a, float b2) { return fmaxf(a, b2); }, sh) > 0.f;
+    if (YH > 0.f) {
+        // live columns: an upper bound of v / E that reaches the chunk's lower bound
+        const float thr = LB * 0.9999f;
+#pragma unroll
+        for (int j = 0; j < EPT2; ++j) {
+            if (rv[j] > 0.f && yhi[j] >= thr) {
+                const int col = base + group_col(j >> 2) + (j & 3);
+                const int slot = atomicAdd(&nlive, 1);
+                if (slot < RB_LIVE) {
+                    const float E = p.e ? fmaxf(p.e[(int64_t)b * p.Vg + col], 1e-10f)
+                                        : fmaxf(-log_fixed(word_to_open_uniform(philox_word(
+                                                    p.seed_lo, p.seed_hi, p.offset, 1u, (uint32_t)b, (uint32_t)col))),
+                                                1e-10f);
+                    live_col[slot] = col;
+                    live_y[slot] = __fdiv_rn(rv[j], E);
+                }
+            }
+        }
+        __syncthreads();
+        const int nl = nlive;
+        if (nl > RB_LIVE) {
+            overflow = true;
+        } else {
+            float ybest = 0.f;
+            for (int i = 0; i < nl; ++i) ybest = fmaxf(ybest, live_y[i]);
+            const float keep_thr = ybest * (1.0f - 1.0f / (1 << 20));
+            if ((int)threadIdx.x < nl && live_y[threadIdx.x] >= keep_thr) {
+                const int slot = atomicAdd(&nkeep, 1);
+                if (slot < RB_CAP) p.cand[((int64_t)b * p.C2 + c) * RB_CAP + slot] = live_col[threadIdx.x];
+            }
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int cnt;
+        if (YH > 0.f || overflow) cnt = (overflow || nkeep > RB_CAP) ? RB_CAP + 1 : nkeep;
+        else {  // every residual of the chunk is 0: its first column stands for all of them
+            p.cand[((int64_t)b * p.C2 + c) * RB_CAP] = base;
+            cnt = 1;
+        }
+        __stcg(p.ncand + b * p.C2 + c, cnt);
+        __stcg(p.rsum + b * p.C2 + c, make_float2(csr, csp));
+        __threadfence();
+        last = atomicAdd(p.counters + b, 1) == p.C2 - 1;
+    }
+    __syncthreads();
+    if (!last) return;
+    // ---- last CTA of sequence b: the normaliser, then the exact values of the candidates
+    __threadfence();
+    if (threadIdx.x < 32) {
+        float s1 = 0.f, s2 = 0.f;
+        for (int cc = lane; cc < p.C2; cc += 32) {
+            const float2 v = __ldcg(p.rsum + b * p.C2 + cc);
+            s1 += v.x;
+            s2 += v.y;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            s1 += __shfl_xor_sync(0xffffffffu, s1, o);
+            s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+        }
+        if (lane == 0) {
+            use_p = !(s1 > 0.f);                   // fallback to p[a], verify.py:151
+            zsh = fmaxf(use_p ? s2 : s1, 1e-10f);  // normaliser, verify.py:152
+        }
+    }
+    __syncthreads();
+    const float Z = zsh;
+    const bool up = use_p != 0;
+    float best = -INFINITY;
+    int bidx = 0x7fffffff;
+    auto eval = [&](auto unit, int i) {
+        float r, pv;
+        resid_of<decltype(unit)::value>(p, d, T, tr.at(i), dr.p ? dr.at(i) : 0.f, r, pv);
+        const float v = up ? pv : r;
+        const float E = p.e ? fmaxf(p.e[(int64_t)b * p.Vg + i], 1e-10f)
+                            : fmaxf(-log_fixed(word_to_open_uniform(
+                                        philox_word(p.seed_lo, p.seed_hi, p.offset, 1u, (uint32_t)b, (uint32_t)i))),
+                                    1e-10f);
+        const float x = v != 0.f ? __fdiv_rn(__fdiv_rn(v, Z), E) : 0.f;  // 0 / Z / E is +0
+        if (better(x, i, best, bidx)) {
+            best = x;
+            bidx = i;
+        }
+    };
+    auto finish = [&](auto unit) {
+        if (up) {  // rare: no residual mass; every column of the row, v = p[a]
+            for (int i = threadIdx.x; i < p.V; i += THREADS) eval(unit, i);
+            return;
+        }
+        // the kept columns of every chunk, (chunk, slot) pairs spread over the threads
+        for (int u = threadIdx.x; u < p.C2 * RB_CAP; u += THREADS) {
+            const int cc = u / RB_CAP, sl = u - cc * RB_CAP;
+            const int cnt = __ldcg(p.ncand + b * p.C2 + cc);
+            if (cnt > RB_CAP) {
+                if (sl == 0) any_ovf = 1;
+            } else if (sl < cnt) {
+                eval(unit, __ldcg(p.cand + ((int64_t)b * p.C2 + cc) * RB_CAP + sl));
+            }
+        }
+        __syncthreads();
+        if (!any_ovf) return;
+        for (int cc = 0; cc < p.C2; ++cc) {  // rare: ties or a flat chunk; all of its columns
+            if (__ldcg(p.ncand + b * p.C2 + cc) <= RB_CAP) continue;
+            const int hi = min(p.V, (cc + 1) * CHUNK2);
+            for (int i = cc * CHUNK2 + threadIdx.x; i < hi; i += THREADS) eval(unit, i);
+        }
+    };
+    if (T == 1.0f) finish(std::true_type{});
+    else finish(std::false_type{});
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bidx, o);
+        if (better(ov, oi, best, bidx)) {
+            best = ov;
+            bidx = oi;
+        }
+    }
+    if (lane == 0) {
+        bv[w] = best;
+        bi[w] = bidx;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int i = 1; i < THREADS / 32; ++i)
+            if (better(bv[i], bi[i], best, bidx)) {
+                best = bv[i];
+                bidx = bi[i];
+            }
+        p.out_bonus[b] = bidx == 0x7fffffff ? 0 : bidx;
+        p.counters[b] = 0;  // graph-replay safe: ready for the next call
+    }
+}
+
 struct WsLayout {
-    size_t err, counters, dec, stats, rsum, amax, total;
+    size_t err, counters, dec, stats, rsum, amax, ncand, cand, total;
 };
 
 constexpr int kCounterCap = 1 << 19;  // sequences per call
@@ -927,6 +1168,10 @@ static WsLayout ws_layout(int B, int k, int Tr, int V) {
     off = align_up(off + sizeof(float2) * (size_t)B * C2, 256);
     w.amax = off;
     off = align_up(off + sizeof(float2) * (size_t)B * C2, 256);
+    w.ncand = off;
+    off = align_up(off + sizeof(int) * (size_t)B * C2, 256);
+    w.cand = off;
+    off = align_up(off + sizeof(int) * (size_t)B * C2 * RB_CAP, 256);
     w.total = off;
     return w;
 }
@@ -1019,6 +1264,8 @@ int setup(vs::Params& p, const void* draft, int draft_dtype, const void* target,
     p.stats = reinterpret_cast<float2*>(ws + w.stats);
     p.rsum = reinterpret_cast<float2*>(ws + w.rsum);
     p.amax = reinterpret_cast<float2*>(ws + w.amax);
+    p.ncand = reinterpret_cast<int*>(ws + w.ncand);
+    p.cand = reinterpret_cast<int*>(ws + w.cand);
     // passes 3-4 read 16-byte vectors when every row they read is 16-byte aligned (the
     // point-mass draft is read too: its residual row) and Philox groups of four columns
     // start on this rank's group boundaries
@@ -1064,6 +1311,10 @@ extern "C" int sdb_verify_batch_ex(const void* draft, int draft_dtype, const voi
     vs::vs_decide<<<B, vs::DECIDE_THREADS, 0, st>>>(p);
     rc = cuda_status(cudaGetLastError(), "vs_decide launch");
     if (rc) return rc;
+    if (p.vec) {  // one pass over row a: sums, candidates, and the bonus by the last CTA
+        vs::vs_resid_bonus<<<dim3(B, p.C2), vs::THREADS, 0, st>>>(p);
+        return cuda_status(cudaGetLastError(), "vs_resid_bonus launch");
+    }
     vs::vs_resid_sums<<<dim3(B, p.C2), vs::THREADS, 0, st>>>(p);
     rc = cuda_status(cudaGetLastError(), "vs_resid_sums launch");
     if (rc) return rc;
