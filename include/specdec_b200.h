@@ -293,6 +293,21 @@ int sdb_verify_batch_ex(const void* draft_logits, int draft_dtype,
                         int B, int k, int target_rows, int V,
                         void* workspace, size_t workspace_bytes, void* stream);
 
+/* Graph-safe form of sdb_verify_batch_ex (draws generated in-kernel): the Philox offset is
+ * read from device memory (*offset_dev, 8-byte aligned) when the kernels run and advanced
+ * by one after the call (a one-thread launch on the same stream), so a call captured in
+ * a CUDA graph draws new values on every replay.  The draws of a call that finds
+ * *offset_dev == v equal those of sdb_verify_batch_ex with offset v.  The reference
+ * draws with torch's generator inside the call (verify.py:120, :209); its eager calls
+ * advance it on every call, which a host-side offset captured in a graph would not. */
+int sdb_verify_batch_dev_offset(const void* draft_logits, int draft_dtype,
+                                const void* target_logits, int target_dtype,
+                                const int64_t* draft_tokens, const float* temperatures,
+                                uint64_t seed, uint64_t* offset_dev, int draft_is_point_mass,
+                                int64_t* out_accepted, int64_t* out_bonus, uint8_t* out_accept_mask,
+                                int B, int k, int target_rows, int V,
+                                void* workspace, size_t workspace_bytes, void* stream);
+
 /* verify_batch over vocabulary shards: the LM head split by columns across tp ranks
  * (ParallelLMHead, nanovllm/layers/embed_head.py:56-75).  The reference gathers the
  * full logits on rank 0 (:71-74); here every rank keeps its shard and the ranks
@@ -351,6 +366,17 @@ int sdb_philox_fill(float* out, int rows, int cols, uint64_t seed, uint64_t offs
  * place).
  * ========================================================================= */
 size_t sdb_sample_workspace_size(int B, int V);
+
+/* Graph-safe form of sdb_sample with in-kernel noise: the Philox offset is read from
+ * device memory (*offset_dev, 8-byte aligned) when the kernels run and advanced by one
+ * after the call, so a captured call samples new noise on every replay (the reference's
+ * exponential_() advances torch's generator, sampler.py:11, draft_proposer.py:508).  A
+ * call that finds *offset_dev == v samples what sdb_sample does with offset v. */
+int sdb_sample_dev_offset(const void* logits, int64_t logits_stride_row, int dtype,
+                          const float* temperatures, uint64_t seed, uint64_t* offset_dev,
+                          int64_t* tokens, int64_t tokens_stride,
+                          float* logits_f32, int64_t logits_f32_stride_row,
+                          int B, int V, void* workspace, size_t workspace_bytes, void* stream);
 int sdb_sample(const void* logits, int64_t logits_stride_row, int dtype,
                const float* temperatures, const float* exponentials,
                uint64_t seed, uint64_t offset,

@@ -85,6 +85,9 @@ SIGNATURES = {
     "sdb_verify_batch_ex": (_c_i32, [
         _c_p, _c_i32, _c_p, _c_i32, _c_p, _c_p, _c_p, _c_p, _c_u64, _c_u64, _c_i32, _c_p, _c_p, _c_p,
         _c_i32, _c_i32, _c_i32, _c_i32, _c_p, _c_sz, _c_p]),
+    "sdb_verify_batch_dev_offset": (_c_i32, [
+        _c_p, _c_i32, _c_p, _c_i32, _c_p, _c_p, _c_u64, _c_p, _c_i32, _c_p, _c_p, _c_p,
+        _c_i32, _c_i32, _c_i32, _c_i32, _c_p, _c_sz, _c_p]),
     "sdb_verify_shard_send_floats": (_c_sz, [_c_i32] * 4),
     "sdb_verify_batch_shard": (_c_i32, [
         _c_i32, _c_p, _c_i32, _c_p, _c_i32, _c_p, _c_p, _c_p, _c_p, _c_u64, _c_u64, _c_i32, _c_p, _c_p, _c_p,
@@ -95,6 +98,9 @@ SIGNATURES = {
         _c_p, _c_i64, _c_i64, _c_p, _c_p, _c_i64, _c_i64, _c_p, _c_p, _c_i64, _c_i64, _c_i64, _c_p,
         _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_i32, _c_p, _c_p]),
     "sdb_sample_workspace_size": (_c_sz, [_c_i32, _c_i32]),
+    "sdb_sample_dev_offset": (_c_i32, [
+        _c_p, _c_i64, _c_i32, _c_p, _c_u64, _c_p, _c_p, _c_i64, _c_p, _c_i64, _c_i32, _c_i32,
+        _c_p, _c_sz, _c_p]),
     "sdb_sample": (_c_i32, [
         _c_p, _c_i64, _c_i32, _c_p, _c_p, _c_u64, _c_u64, _c_p, _c_i64, _c_p, _c_i64, _c_i32, _c_i32,
         _c_p, _c_sz, _c_p]),

@@ -27,6 +27,8 @@ int device_sm_count();
 int device_index();
 // Dynamic shared memory opt-in, done once per (device, kernel).
 int ensure_smem_attr(const void* func, int bytes, int slot);
+// One-thread launch that adds 1 to a device-resident uint64 Philox offset.
+int launch_advance_offset(uint64_t* off, cudaStream_t st);
 
 // Tensor-map encoder obtained from the driver through the runtime.
 int encode_tensor_map(CUtensorMap* map, CUtensorMapDataType dtype, cuuint32_t rank,

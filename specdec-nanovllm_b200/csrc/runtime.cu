@@ -76,9 +76,71 @@ static PFN_cuTensorMapEncodeTiled_v12000 get_encoder() {
     return fn;
 }
 
+namespace {
+// Recently encoded tensor maps of this host thread.  A map is a pure function of its
+// arguments (the remaining encode options are fixed here), so a launch that repeats the
+// arguments of a recent one -- every decode / verify step of a serving loop -- reuses it
+// instead of calling the driver again.
+struct MapKey {
+    int dtype, rank, swizzle;
+    void* base;
+    cuuint64_t dims[5], strides[4];
+    cuuint32_t box[5];
+};
+struct MapEntry {
+    MapKey key;
+    CUtensorMap map;
+    bool used;
+};
+constexpr int kMapCache = 16;
+thread_local MapEntry t_maps[kMapCache];
+thread_local int t_next_map = 0;
+
+bool same_key(const MapKey& a, const MapKey& b) {
+    if (a.dtype != b.dtype || a.rank != b.rank || a.swizzle != b.swizzle || a.base != b.base) return false;
+    for (int i = 0; i < a.rank; ++i)
+        if (a.dims[i] != b.dims[i] || a.box[i] != b.box[i] || (i + 1 < a.rank && a.strides[i] != b.strides[i]))
+            return false;
+    return true;
+}
+}  // namespace
+
+int encode_tensor_map_uncached(CUtensorMap* map, CUtensorMapDataType dtype, cuuint32_t rank, void* base,
+                               const cuuint64_t* dims, const cuuint64_t* strides_bytes, const cuuint32_t* box,
+                               CUtensorMapSwizzle swizzle);
+
 int encode_tensor_map(CUtensorMap* map, CUtensorMapDataType dtype, cuuint32_t rank, void* base,
                       const cuuint64_t* dims, const cuuint64_t* strides_bytes, const cuuint32_t* box,
                       CUtensorMapSwizzle swizzle) {
+    if (rank < 1 || rank > 5) return encode_tensor_map_uncached(map, dtype, rank, base, dims, strides_bytes, box, swizzle);
+    MapKey k{};
+    k.dtype = (int)dtype;
+    k.rank = (int)rank;
+    k.swizzle = (int)swizzle;
+    k.base = base;
+    for (cuuint32_t i = 0; i < rank; ++i) {
+        k.dims[i] = dims[i];
+        k.box[i] = box[i];
+        if (i + 1 < rank) k.strides[i] = strides_bytes[i];
+    }
+    for (int i = 0; i < kMapCache; ++i)
+        if (t_maps[i].used && same_key(t_maps[i].key, k)) {
+            *map = t_maps[i].map;
+            return SDB_OK;
+        }
+    const int rc = encode_tensor_map_uncached(map, dtype, rank, base, dims, strides_bytes, box, swizzle);
+    if (rc) return rc;
+    MapEntry& e = t_maps[t_next_map];
+    t_next_map = (t_next_map + 1) % kMapCache;
+    e.key = k;
+    e.map = *map;
+    e.used = true;
+    return SDB_OK;
+}
+
+int encode_tensor_map_uncached(CUtensorMap* map, CUtensorMapDataType dtype, cuuint32_t rank, void* base,
+                               const cuuint64_t* dims, const cuuint64_t* strides_bytes, const cuuint32_t* box,
+                               CUtensorMapSwizzle swizzle) {
     auto enc = get_encoder();
     if (!enc) {
         set_last_error("cuTensorMapEncodeTiled is not available from the driver");
@@ -95,6 +157,16 @@ int encode_tensor_map(CUtensorMap* map, CUtensorMapDataType dtype, cuuint32_t ra
     return SDB_OK;
 }
 
+}  // namespace sdb
+
+namespace sdb {
+// Advances a device-resident Philox offset after the call that read it (the graph-safe
+// sampling entry points): stream order puts it after every kernel of that call.
+__global__ void advance_offset_kernel(uint64_t* off) { *off += 1; }
+int launch_advance_offset(uint64_t* off, cudaStream_t st) {
+    advance_offset_kernel<<<1, 1, 0, st>>>(off);
+    return cuda_status(cudaGetLastError(), "advance_offset launch");
+}
 }  // namespace sdb
 
 extern "C" const char* sdb_last_error(void) { return sdb::g_last_error; }

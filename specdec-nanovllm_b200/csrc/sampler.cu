@@ -60,6 +60,7 @@ struct Params {
     const float* temps;      // (B) or null
     const float* e;          // (B, V) or null
     uint32_t seed_lo, seed_hi, offset;
+    const uint64_t* offset_dev;  // graph-safe form: the offset read from device memory
     float* copy;             // fp32 copy of the logits (B rows of stride cs) or null
     int64_t cs;
     int64_t* tokens;         // token of row b at tokens[b * ts]
@@ -81,6 +82,10 @@ template <>
 SDB_DEV float to_f32<__half>(__half v) { return __half2float(v); }
 
 SDB_DEV bool better(float v, int i, float bv, int bi) { return v > bv || (v == bv && i < bi); }
+
+// The Philox offset of this call: the host value, or the device-resident one of the
+// graph-safe entry point (unchanged while the call's kernels run).
+SDB_DEV uint32_t draw_offset(const Params& p) { return p.offset_dev ? (uint32_t)*p.offset_dev : p.offset; }
 
 template <typename F>
 SDB_DEV float block_reduce(float v, F op, float* sh) {
@@ -204,7 +209,7 @@ __global__ void __launch_bounds__(THREADS) smp_chunk(const Params p) {
             w4[0] = (uint32_t)i0 >> 2;
             w4[1] = (uint32_t)b;
             w4[2] = 2u;
-            w4[3] = p.offset;
+            w4[3] = draw_offset(p);
             philox(w4, p.seed_lo, p.seed_hi);
         }
 #pragma unroll
@@ -219,7 +224,7 @@ __global__ void __launch_bounds__(THREADS) smp_chunk(const Params p) {
             if (p.e) {
                 Elo = i < p.V ? fmaxf(p.e[(int64_t)b * p.V + i], 1e-10f) : 1.f;
             } else {
-                if (!vec) w = i < p.V ? philox_word(p.seed_lo, p.seed_hi, p.offset, 2u, (uint32_t)b, (uint32_t)i) : 0u;
+                if (!vec) w = i < p.V ? philox_word(p.seed_lo, p.seed_hi, draw_offset(p), 2u, (uint32_t)b, (uint32_t)i) : 0u;
                 Elo = fmaxf((float)(0xFFFFFFu - (w >> 8)) * (5.9604644775390625e-08f * 0.99999f), 1e-10f);
             }
             ub[j] = __fdividef(a * (1.f + kBand), Elo);
@@ -260,7 +265,7 @@ __global__ void __launch_bounds__(THREADS) smp_chunk(const Params p) {
         col2 = live_col[threadIdx.x];
         const float a = live_a[threadIdx.x];
         const float E = p.e ? fmaxf(p.e[(int64_t)b * p.V + col2], 1e-10f)
-                            : exp_draw(philox_word(p.seed_lo, p.seed_hi, p.offset, 2u, (uint32_t)b, (uint32_t)col2));
+                            : exp_draw(philox_word(p.seed_lo, p.seed_hi, draw_offset(p), 2u, (uint32_t)b, (uint32_t)col2));
         lb2 = __fdividef(a * (1.f - kBand), E);
         ub2 = __fdividef(a * (1.f + kBand), E);
     }
@@ -306,7 +311,7 @@ __global__ void __launch_bounds__(PICK_WARPS * 32) smp_pick(const Params p) {
         float xt = to_f32<T>(row[i]);
         if (T_ != 1.0f) xt = __fdiv_rn(xt, T_);
         const float E = p.e ? fmaxf(p.e[(int64_t)b * p.V + i], 1e-10f)
-                            : exp_draw(philox_word(p.seed_lo, p.seed_hi, p.offset, 2u, (uint32_t)b, (uint32_t)i));
+                            : exp_draw(philox_word(p.seed_lo, p.seed_hi, draw_offset(p), 2u, (uint32_t)b, (uint32_t)i));
         const float v = __fdiv_rn(__fdiv_rn(expf(xt - m), S), E);
         if (better(v, i, best, bidx)) {
             best = v;
@@ -384,10 +389,11 @@ extern "C" size_t sdb_sample_workspace_size(int B, int V) {
     return smp::ws_layout(B, V).total;
 }
 
-extern "C" int sdb_sample(const void* logits, int64_t logits_stride_row, int dtype, const float* temperatures,
-                          const float* exponentials, uint64_t seed, uint64_t offset, int64_t* tokens,
-                          int64_t tokens_stride, float* logits_f32, int64_t logits_f32_stride_row, int B, int V,
-                          void* workspace, size_t workspace_bytes, void* stream) {
+namespace {
+int sample_impl(const void* logits, int64_t logits_stride_row, int dtype, const float* temperatures,
+                const float* exponentials, uint64_t seed, uint64_t offset, uint64_t* offset_dev, int64_t* tokens,
+                int64_t tokens_stride, float* logits_f32, int64_t logits_f32_stride_row, int B, int V,
+                void* workspace, size_t workspace_bytes, void* stream) {
     if (B == 0) return SDB_OK;
     if (!logits || !tokens || !workspace || B < 0 || V <= 0 || logits_stride_row < V || tokens_stride < 1 ||
         (logits_f32 && logits_f32_stride_row < V) ||
@@ -431,8 +437,34 @@ extern "C" int sdb_sample(const void* logits, int64_t logits_stride_row, int dty
     p.stats = reinterpret_cast<float2*>(ws + w.stats);
     p.ncand = reinterpret_cast<int*>(ws + w.ncand);
     p.cand = reinterpret_cast<int*>(ws + w.cand);
+    p.offset_dev = offset_dev;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    if (dtype == SDB_F32) return smp::launch<float>(p, st);
-    if (dtype == SDB_BF16) return smp::launch<__nv_bfloat16>(p, st);
-    return smp::launch<__half>(p, st);
+    int rc;
+    if (dtype == SDB_F32) rc = smp::launch<float>(p, st);
+    else if (dtype == SDB_BF16) rc = smp::launch<__nv_bfloat16>(p, st);
+    else rc = smp::launch<__half>(p, st);
+    if (rc || !offset_dev) return rc;
+    return launch_advance_offset(offset_dev, st);
+}
+}  // namespace
+
+extern "C" int sdb_sample(const void* logits, int64_t logits_stride_row, int dtype, const float* temperatures,
+                          const float* exponentials, uint64_t seed, uint64_t offset, int64_t* tokens,
+                          int64_t tokens_stride, float* logits_f32, int64_t logits_f32_stride_row, int B, int V,
+                          void* workspace, size_t workspace_bytes, void* stream) {
+    return sample_impl(logits, logits_stride_row, dtype, temperatures, exponentials, seed, offset, nullptr, tokens,
+                       tokens_stride, logits_f32, logits_f32_stride_row, B, V, workspace, workspace_bytes, stream);
+}
+
+extern "C" int sdb_sample_dev_offset(const void* logits, int64_t logits_stride_row, int dtype,
+                                     const float* temperatures, uint64_t seed, uint64_t* offset_dev,
+                                     int64_t* tokens, int64_t tokens_stride, float* logits_f32,
+                                     int64_t logits_f32_stride_row, int B, int V, void* workspace,
+                                     size_t workspace_bytes, void* stream) {
+    if (!offset_dev || (reinterpret_cast<uintptr_t>(offset_dev) & 7)) {
+        set_last_error("sdb_sample_dev_offset needs an 8-byte aligned device offset");
+        return SDB_ERR_INVALID_ARG;
+    }
+    return sample_impl(logits, logits_stride_row, dtype, temperatures, nullptr, seed, 0, offset_dev, tokens,
+                       tokens_stride, logits_f32, logits_f32_stride_row, B, V, workspace, workspace_bytes, stream);
 }

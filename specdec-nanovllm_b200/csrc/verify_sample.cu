@@ -62,6 +62,7 @@ struct Params {
     const float* u;        // (B, k) or null
     const float* e;        // (B, V) or null
     uint32_t seed_lo, seed_hi, offset;
+    const uint64_t* offset_dev;  // graph-safe form: the offset read from device memory
     int point_mass;
     int64_t* out_acc;
     int64_t* out_bonus;
@@ -84,9 +85,13 @@ struct Params {
     float* send;
 };
 
+// The Philox offset of this call: the host value, or the device-resident one of the
+// graph-safe entry point (unchanged while the call's kernels run).
+SDB_DEV uint32_t draw_offset(const Params& p) { return p.offset_dev ? (uint32_t)*p.offset_dev : p.offset; }
+
 SDB_DEV float accept_uniform(const Params& p, int b, int j) {
     if (p.u) return p.u[b * p.k + j];
-    return word_to_uniform(philox_word(p.seed_lo, p.seed_hi, p.offset, 0u, (uint32_t)b, (uint32_t)j));
+    return word_to_uniform(philox_word(p.seed_lo, p.seed_hi, draw_offset(p), 0u, (uint32_t)b, (uint32_t)j));
 }
 
 // x / T exactly as torch divides (IEEE); T == 1 is the identity.
@@ -690,12 +695,12 @@ SDB_DEV void exp_noise4(const Params& p, int b, int i, int cnt, float (&E)[4]) {
 #pragma unroll
         for (int e = 0; e < 4; ++e) E[e] = e < cnt ? p.e[(int64_t)b * p.Vg + i + e] : 1.f;
     } else if (cnt == 4) {
-        uint32_t c[4] = {(uint32_t)i >> 2, (uint32_t)b, 1u, p.offset};
+        uint32_t c[4] = {(uint32_t)i >> 2, (uint32_t)b, 1u, draw_offset(p)};
         philox(c, p.seed_lo, p.seed_hi);
 #pragma unroll
         for (int e = 0; e < 4; ++e) E[e] = -log_fixed(word_to_open_uniform(c[e]));
     } else {
-        E[0] = -log_fixed(word_to_open_uniform(philox_word(p.seed_lo, p.seed_hi, p.offset, 1u, (uint32_t)b, (uint32_t)i)));
+        E[0] = -log_fixed(word_to_open_uniform(philox_word(p.seed_lo, p.seed_hi, draw_offset(p), 1u, (uint32_t)b, (uint32_t)i)));
     }
 #pragma unroll
     for (int e = 0; e < 4; ++e) E[e] = fmaxf(E[e], 1e-10f);  // clamp_min_(1e-10), verify.py:209
@@ -797,7 +802,7 @@ __global__ void __launch_bounds__(THREADS) vs_bonus(const Params p) {
             const bool in = idx < n;
             const float t4[4] = {xt[q].x, xt[q].y, xt[q].z, xt[q].w};
             const float d4[4] = {xd[q].x, xd[q].y, xd[q].z, xd[q].w};
-            uint32_t w4[4] = {(uint32_t)(p.col0 + base + idx) >> 2, (uint32_t)b, 1u, p.offset};
+            uint32_t w4[4] = {(uint32_t)(p.col0 + base + idx) >> 2, (uint32_t)b, 1u, draw_offset(p)};
             if (!p.e && in) philox(w4, p.seed_lo, p.seed_hi);
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
@@ -843,7 +848,7 @@ __global__ void __launch_bounds__(THREADS) vs_bonus(const Params p) {
             const int i = base + group_col(j >> 2) + (j & 3);
             const float E = p.e ? fmaxf(p.e[(int64_t)b * p.Vg + p.col0 + i], 1e-10f)
                                 : fmaxf(-log_fixed(word_to_open_uniform(philox_word(
-                                            p.seed_lo, p.seed_hi, p.offset, 1u, (uint32_t)b, (uint32_t)(p.col0 + i)))),
+                                            p.seed_lo, p.seed_hi, draw_offset(p), 1u, (uint32_t)b, (uint32_t)(p.col0 + i)))),
                                         1e-10f);
             exact(unit, i, tr.at(i), dr.p ? dr.at(i) : 0.f, E);
         }
@@ -969,7 +974,7 @@ __global__ void __launch_bounds__(THREADS) vs_resid_bonus(const Params p) {
             const bool in = idx < n;
             const float t4[4] = {xt[q].x, xt[q].y, xt[q].z, xt[q].w};
             const float d4[4] = {xd[q].x, xd[q].y, xd[q].z, xd[q].w};
-            uint32_t w4[4] = {(uint32_t)(base + idx) >> 2, (uint32_t)b, 1u, p.offset};
+            uint32_t w4[4] = {(uint32_t)(base + idx) >> 2, (uint32_t)b, 1u, draw_offset(p)};
             if (!p.e && in) philox(w4, p.seed_lo, p.seed_hi);
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
@@ -1021,7 +1026,7 @@ __global__ void __launch_bounds__(THREADS) vs_resid_bonus(const Params p) {
                 if (slot < RB_LIVE) {
                     const float E = p.e ? fmaxf(p.e[(int64_t)b * p.Vg + col], 1e-10f)
                                         : fmaxf(-log_fixed(word_to_open_uniform(philox_word(
-                                                    p.seed_lo, p.seed_hi, p.offset, 1u, (uint32_t)b, (uint32_t)col))),
+                                                    p.seed_lo, p.seed_hi, draw_offset(p), 1u, (uint32_t)b, (uint32_t)col))),
                                                 1e-10f);
                     live_col[slot] = col;
                     live_y[slot] = __fdiv_rn(rv[j], E);
@@ -1087,7 +1092,7 @@ __global__ void __launch_bounds__(THREADS) vs_resid_bonus(const Params p) {
         const float v = up ? pv : r;
         const float E = p.e ? fmaxf(p.e[(int64_t)b * p.Vg + i], 1e-10f)
                             : fmaxf(-log_fixed(word_to_open_uniform(
-                                        philox_word(p.seed_lo, p.seed_hi, p.offset, 1u, (uint32_t)b, (uint32_t)i))),
+                                        philox_word(p.seed_lo, p.seed_hi, draw_offset(p), 1u, (uint32_t)b, (uint32_t)i))),
                                     1e-10f);
         const float x = v != 0.f ? __fdiv_rn(__fdiv_rn(v, Z), E) : 0.f;  // 0 / Z / E is +0
         if (better(x, i, best, bidx)) {
@@ -1296,16 +1301,47 @@ int launch_stats(const vs::Params& p, cudaStream_t st) {
 
 }  // namespace
 
+namespace {
+int verify_impl(const void* draft, int draft_dtype, const void* target, int target_dtype, const int64_t* tokens,
+                const float* temps, const float* uniforms, const float* exponentials, uint64_t seed, uint64_t offset,
+                uint64_t* offset_dev, int point_mass, int64_t* out_acc, int64_t* out_bonus, uint8_t* out_mask, int B,
+                int k, int Tr, int V, void* workspace, size_t workspace_bytes, cudaStream_t st);
+}  // namespace
+
 extern "C" int sdb_verify_batch_ex(const void* draft, int draft_dtype, const void* target, int target_dtype,
                                    const int64_t* tokens, const float* temps, const float* uniforms,
                                    const float* exponentials, uint64_t seed, uint64_t offset, int point_mass,
                                    int64_t* out_acc, int64_t* out_bonus, uint8_t* out_mask, int B, int k, int Tr,
                                    int V, void* workspace, size_t workspace_bytes, void* stream) {
+    return verify_impl(draft, draft_dtype, target, target_dtype, tokens, temps, uniforms, exponentials, seed, offset,
+                       nullptr, point_mass, out_acc, out_bonus, out_mask, B, k, Tr, V, workspace, workspace_bytes,
+                       reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int sdb_verify_batch_dev_offset(const void* draft, int draft_dtype, const void* target, int target_dtype,
+                                           const int64_t* tokens, const float* temps, uint64_t seed,
+                                           uint64_t* offset_dev, int point_mass, int64_t* out_acc,
+                                           int64_t* out_bonus, uint8_t* out_mask, int B, int k, int Tr, int V,
+                                           void* workspace, size_t workspace_bytes, void* stream) {
+    if (!offset_dev || (reinterpret_cast<uintptr_t>(offset_dev) & 7)) {
+        set_last_error("sdb_verify_batch_dev_offset needs an 8-byte aligned device offset");
+        return SDB_ERR_INVALID_ARG;
+    }
+    return verify_impl(draft, draft_dtype, target, target_dtype, tokens, temps, nullptr, nullptr, seed, 0, offset_dev,
+                       point_mass, out_acc, out_bonus, out_mask, B, k, Tr, V, workspace, workspace_bytes,
+                       reinterpret_cast<cudaStream_t>(stream));
+}
+
+namespace {
+int verify_impl(const void* draft, int draft_dtype, const void* target, int target_dtype, const int64_t* tokens,
+                const float* temps, const float* uniforms, const float* exponentials, uint64_t seed, uint64_t offset,
+                uint64_t* offset_dev, int point_mass, int64_t* out_acc, int64_t* out_bonus, uint8_t* out_mask, int B,
+                int k, int Tr, int V, void* workspace, size_t workspace_bytes, cudaStream_t st) {
     vs::Params p;
     int rc = setup(p, draft, draft_dtype, target, target_dtype, tokens, temps, uniforms, exponentials, seed, offset,
                    point_mass, out_acc, out_bonus, out_mask, B, k, Tr, V, 0, V, workspace, workspace_bytes);
     if (rc) return rc;
-    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    p.offset_dev = offset_dev;
     rc = launch_stats(p, st);
     if (rc) return rc;
     vs::vs_decide<<<B, vs::DECIDE_THREADS, 0, st>>>(p);
@@ -1313,14 +1349,18 @@ extern "C" int sdb_verify_batch_ex(const void* draft, int draft_dtype, const voi
     if (rc) return rc;
     if (p.vec) {  // one pass over row a: sums, candidates, and the bonus by the last CTA
         vs::vs_resid_bonus<<<dim3(B, p.C2), vs::THREADS, 0, st>>>(p);
-        return cuda_status(cudaGetLastError(), "vs_resid_bonus launch");
+        rc = cuda_status(cudaGetLastError(), "vs_resid_bonus launch");
+    } else {
+        vs::vs_resid_sums<<<dim3(B, p.C2), vs::THREADS, 0, st>>>(p);
+        rc = cuda_status(cudaGetLastError(), "vs_resid_sums launch");
+        if (rc) return rc;
+        vs::vs_bonus<<<dim3(B, p.C2), vs::THREADS, 0, st>>>(p);
+        rc = cuda_status(cudaGetLastError(), "vs_bonus launch");
     }
-    vs::vs_resid_sums<<<dim3(B, p.C2), vs::THREADS, 0, st>>>(p);
-    rc = cuda_status(cudaGetLastError(), "vs_resid_sums launch");
-    if (rc) return rc;
-    vs::vs_bonus<<<dim3(B, p.C2), vs::THREADS, 0, st>>>(p);
-    return cuda_status(cudaGetLastError(), "vs_bonus launch");
+    if (rc || !offset_dev) return rc;
+    return launch_advance_offset(offset_dev, st);
 }
+}  // namespace
 
 extern "C" size_t sdb_verify_shard_send_floats(int B, int k, int target_rows, int phase) {
     if (B <= 0 || k <= 0 || target_rows <= 0) return 0;

@@ -34,12 +34,15 @@ def workspace_bytes(B: int, V: int) -> int:
 def sample(logits: torch.Tensor, temperatures: Optional[torch.Tensor] = None, *,
            exponentials: Optional[torch.Tensor] = None, seed: Optional[int] = None,
            offset: Optional[int] = None, out: Optional[torch.Tensor] = None,
-           logits_out: Optional[torch.Tensor] = None) -> torch.Tensor:
+           logits_out: Optional[torch.Tensor] = None,
+           offset_tensor: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Tokens (B,) int64 for logits (B, V) fp32 / bf16 / fp16 (rows may be strided).
 
     ``temperatures`` (B,) (or (B, 1)) float32, > 0 as in the reference; None = 1.
     ``out``: int64 destination with B elements, any stride (e.g. ``cands[:, s]``).
     ``logits_out``: (B, V) float32 destination of ``logits.float()`` (any row stride).
+    ``offset_tensor``: a one-element int64 CUDA tensor holding the Philox offset, read when
+    the kernels run and advanced by one after the call (graph-safe in-kernel noise).
     """
     _lib.require_cuda(logits)
     if logits.dim() != 2:
@@ -72,6 +75,18 @@ def sample(logits: torch.Tensor, temperatures: Optional[torch.Tensor] = None, *,
         offset = next(_offsets)
     need = workspace_bytes(B, V)
     ws = _lib.WORKSPACES.get(logits.device, "sample", need)
+    if offset_tensor is not None:
+        if e is not None:
+            raise ValueError("offset_tensor draws in-kernel: no exponentials")
+        if offset_tensor.dtype != torch.int64 or offset_tensor.numel() != 1 or not offset_tensor.is_cuda:
+            raise ValueError("offset_tensor must be a one-element int64 CUDA tensor")
+        rc = _lib.lib().sdb_sample_dev_offset(
+            logits.data_ptr(), logits.stride(0), _lib.DTYPE_CODE[logits.dtype], _lib.ptr(temps),
+            int(seed) & (2**64 - 1), offset_tensor.data_ptr(), out.data_ptr(), out.stride(0),
+            _lib.ptr(logits_out), logits_out.stride(0) if logits_out is not None else 0, B, V,
+            ws.data_ptr(), ws.numel(), _lib.stream_of(logits))
+        _lib.check(rc, "sdb_sample_dev_offset")
+        return out
     rc = _lib.lib().sdb_sample(
         logits.data_ptr(), logits.stride(0), _lib.DTYPE_CODE[logits.dtype], _lib.ptr(temps), _lib.ptr(e),
         int(seed) & (2**64 - 1), int(offset) & (2**64 - 1), out.data_ptr(), out.stride(0),
@@ -91,11 +106,12 @@ class Sampler(nn.Module):
 def draft_sample_step(logits: torch.Tensor, temps: torch.Tensor, out_logits: torch.Tensor,
                       cands: torch.Tensor, s: int, *, seed: Optional[int] = None,
                       offset: Optional[int] = None,
-                      exponentials: Optional[torch.Tensor] = None) -> torch.Tensor:
+                      exponentials: Optional[torch.Tensor] = None,
+                      offset_tensor: Optional[torch.Tensor] = None) -> torch.Tensor:
     """One step of ``draft_proposer.py:505-510`` in one launch pair: ``out_logits[:, s]``
     = logits.float(), ``cands[:, s]`` = the sampled tokens, which are also returned
     (a view, ready to feed the next step's forward)."""
     dst = cands[:, s]
     sample(logits, temps, exponentials=exponentials, seed=seed, offset=offset, out=dst,
-           logits_out=out_logits[:, s])
+           logits_out=out_logits[:, s], offset_tensor=offset_tensor)
     return dst

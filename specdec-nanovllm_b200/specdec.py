@@ -18,10 +18,11 @@ rotary / KV store (``qk_norm_rope_store``), the paged decode or verify attention
 draft sampler and ``verify_batch`` -- and the residual RMSNorm and SiLU * up of ``layers.py``
 (``layers/layernorm.py``, ``layers/activation.py``) -- around bf16 cuBLAS GEMMs for the
 projections and the LM head (``torch.nn.functional.linear``, the reference's
-``F.linear``) and torch's embedding lookup.  The draft's k steps are one captured CUDA graph and so is
-the target's verify forward (the reference captures both, ``model_runner.py:1218-1347``).
-The draft noise inside the graph comes from torch's generator, which advances on every
-replay; ``verify_batch`` runs after the graph with a fresh Philox offset per step.
+``F.linear``) and torch's embedding lookup.  The draft's k steps are one captured CUDA
+graph, and the target's verify forward with ``verify_batch`` is another (the reference
+captures both forwards, ``model_runner.py:1218-1347``).  The draws inside the graphs
+(the draft noise, the acceptance uniforms and the bonus noise) come from Philox offsets
+kept on the device, which each call reads and advances, so every replay draws anew.
 
 Models are random-init (there are no checkpoints): weights N(0, 0.02) in bf16, norm
 weights 1, tied embeddings.  The KV caches start filled with N(0, 1) values standing for
@@ -41,7 +42,7 @@ from .layers import rms_norm as layer_rms_norm
 from .layers import silu_and_mul
 from .prologue import qk_norm_rope_store, rope_cos_sin_cache
 from .sampler import draft_sample_step
-from .verify import verify_batch
+from .verify import VerifyResult, verify_batch
 
 
 @dataclass(frozen=True)
@@ -170,7 +171,15 @@ class SpecDecodeStep:
         self.cands = torch.empty(B, k, dtype=torch.int64, device=device)
         self.v_ids = torch.empty(B, k + 1, dtype=torch.int64, device=device)
         self.target_logits = None
-        self.noise = torch.empty(B, V, device=device)
+        # Philox offsets of the draft sampler and of verify_batch, on the device: each call
+        # reads its offset and advances it, so every graph replay draws new values
+        self.sample_offset = torch.zeros(1, dtype=torch.int64, device=device)
+        self.verify_offset = torch.zeros(1, dtype=torch.int64, device=device)
+        self.result = VerifyResult(accepted=torch.empty(B, dtype=torch.int64, device=device),
+                                   bonus=torch.empty(B, dtype=torch.int64, device=device),
+                                   n_proposed=torch.full((B,), k, dtype=torch.int64, device=device),
+                                   accept_mask=torch.empty(B, k, dtype=torch.bool, device=device))
+        self.seed = 1234 + seed
         self.n_steps = 0
         self.use_graphs = use_graphs
         self.g_draft = self.g_target = None
@@ -182,8 +191,8 @@ class SpecDecodeStep:
             h = self.d.forward(tok, self.d_pos[s], self.d_slots[s], self.block_tables, self.d_lens[s], 1,
                                self.d_cache)
             lg = self.d.logits(h)
-            self.noise.exponential_(1.0)
-            tok = draft_sample_step(lg, self.temps, self.draft_logits, self.cands, s, exponentials=self.noise)
+            tok = draft_sample_step(lg, self.temps, self.draft_logits, self.cands, s, seed=self.seed,
+                                    offset_tensor=self.sample_offset)
 
     def _verify_forward(self):
         self.v_ids[:, 0] = self.last_tokens
@@ -191,6 +200,8 @@ class SpecDecodeStep:
         h = self.t.forward(self.v_ids.view(-1), self.v_pos, self.v_slots, self.block_tables, self.v_lens,
                            self.k + 1, self.t_cache)
         self.target_logits = self.t.logits(h).view(self.B, self.k + 1, -1)
+        verify_batch(self.draft_logits, self.target_logits, self.cands, self.temps.view(-1), seed=self.seed,
+                     offset_tensor=self.verify_offset, out=self.result)
 
     def _capture(self, fn):
         g = torch.cuda.CUDAGraph()
@@ -212,7 +223,8 @@ class SpecDecodeStep:
             self.g_target = self._capture(self._verify_forward)
             self.graph_target_logits = self.target_logits  # the graph's output buffer
 
-    def step(self):
+    def step(self) -> VerifyResult:
+        """One step; the result (accepted counts, bonus tokens) is the step's device buffer."""
         if self.use_graphs:
             self.g_draft.replay()
             self.g_target.replay()
@@ -221,8 +233,7 @@ class SpecDecodeStep:
             self._propose()
             self._verify_forward()
         self.n_steps += 1
-        return verify_batch(self.draft_logits, self.target_logits, self.cands, self.temps.view(-1),
-                            seed=1234, offset=self.n_steps)
+        return self.result
 
     def close(self):
         self.g_draft = self.g_target = None

@@ -41,9 +41,15 @@ def verify_batch(draft_probs: torch.Tensor, target_logits: torch.Tensor, draft_t
                  temperatures: Optional[torch.Tensor] = None, draft_is_point_mass: bool = False, *,
                  uniforms: Optional[torch.Tensor] = None, exponentials: Optional[torch.Tensor] = None,
                  seed: Optional[int] = None, offset: Optional[int] = None,
-                 out: Optional[VerifyResult] = None) -> VerifyResult:
+                 out: Optional[VerifyResult] = None,
+                 offset_tensor: Optional[torch.Tensor] = None) -> VerifyResult:
     """draft_probs (B, k, V): raw draft logits (probabilities if ``draft_is_point_mass``);
-    target_logits (B, k+1, V) (or (B, k, V)); draft_tokens (B, k); temperatures (B,) or None."""
+    target_logits (B, k+1, V) (or (B, k, V)); draft_tokens (B, k); temperatures (B,) or None.
+
+    ``offset_tensor``: a one-element int64 CUDA tensor holding the Philox offset, read when
+    the kernels run and advanced by one after the call, so a call captured in a CUDA graph
+    draws new values on every replay (in-kernel draws only: no ``uniforms`` /
+    ``exponentials``, no ``offset``)."""
     _lib.require_cuda(draft_probs, target_logits, draft_tokens, temperatures, uniforms, exponentials)
     B, k, V = draft_probs.shape
     Tr = target_logits.shape[1]
@@ -75,6 +81,18 @@ def verify_batch(draft_probs: torch.Tensor, target_logits: torch.Tensor, draft_t
     L = _lib.lib()
     need = int(L.sdb_verify_workspace_size(B, k, Tr, V))
     ws = _lib.WORKSPACES.get(draft.device, "verify", need)
+    if offset_tensor is not None:
+        if u is not None or e is not None:
+            raise ValueError("offset_tensor draws in-kernel: no uniforms / exponentials")
+        if offset_tensor.dtype != torch.int64 or offset_tensor.numel() != 1 or not offset_tensor.is_cuda:
+            raise ValueError("offset_tensor must be a one-element int64 CUDA tensor")
+        rc = L.sdb_verify_batch_dev_offset(
+            draft.data_ptr(), _lib.DTYPE_CODE[draft.dtype], target.data_ptr(), _lib.DTYPE_CODE[target.dtype],
+            tokens.data_ptr(), _lib.ptr(temps), int(seed) & (2**64 - 1), offset_tensor.data_ptr(),
+            1 if draft_is_point_mass else 0, out.accepted.data_ptr(), out.bonus.data_ptr(),
+            out.accept_mask.data_ptr(), B, k, Tr, V, ws.data_ptr(), ws.numel(), _lib.stream_of(draft))
+        _lib.check(rc, "sdb_verify_batch_dev_offset")
+        return out
     rc = L.sdb_verify_batch_ex(draft.data_ptr(), _lib.DTYPE_CODE[draft.dtype], target.data_ptr(),
                                _lib.DTYPE_CODE[target.dtype], tokens.data_ptr(), _lib.ptr(temps),
                                _lib.ptr(u), _lib.ptr(e), int(seed) & (2**64 - 1), int(offset) & (2**64 - 1),

@@ -117,3 +117,32 @@ def test_frequencies_follow_softmax(pkg):
     freq = torch.bincount(tok, minlength=V).float().cpu() / B
     p = torch.softmax(base / T, -1)
     assert torch.allclose(freq, p, atol=5.0 * float(p.max()) ** 0.5 / B ** 0.5)
+
+
+def test_device_offset_noise_equals_host_offset_and_advances_in_graphs(pkg):
+    """sdb_sample_dev_offset: the noise offset lives on the device and advances after each
+    call, so a captured draft sampling step samples new noise on every replay."""
+    g0 = torch.Generator(device="cuda").manual_seed(4)
+    logits = (torch.randn(16, 30000, generator=g0, device="cuda") * 2.0).to(torch.bfloat16)
+    off = torch.tensor([11], dtype=torch.int64, device="cuda")
+    tok = pkg.sample(logits, None, seed=9, offset_tensor=off)
+    want = pkg.sample(logits, None, seed=9, offset=11)
+    torch.cuda.synchronize()
+    assert torch.equal(tok, want) and int(off.item()) == 12
+    out = torch.empty(16, dtype=torch.int64, device="cuda")
+    g = torch.cuda.CUDAGraph()
+    st = torch.cuda.Stream()
+    st.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(st):
+        with torch.cuda.graph(g, stream=st):
+            pkg.sample(logits, None, seed=9, offset_tensor=off, out=out)
+    torch.cuda.current_stream().wait_stream(st)
+    seen = []
+    for v in (12, 13, 14):
+        g.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, pkg.sample(logits, None, seed=9, offset=v)), v
+        seen.append(out.clone())
+    assert not torch.equal(seen[0], seen[1])  # new noise on every replay
+    assert int(off.item()) == 15
+    del g

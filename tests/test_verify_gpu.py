@@ -319,3 +319,33 @@ def test_vocab_parallel_injected_draws_match_oracle(pkg, golden):
         assert np.array_equal(r.accepted.cpu().numpy(), g["accepted"])
         assert np.array_equal(r.accept_mask.cpu().numpy(), g["accept_mask"])
         assert np.array_equal(r.bonus.cpu().numpy(), g["bonus"])
+
+
+def test_device_offset_draws_equal_host_offset_and_advance_in_graphs(pkg):
+    """sdb_verify_batch_dev_offset: the offset is read on the device and advanced after the
+    call, so a captured call draws new values on every replay, each replay equal to the
+    host-offset call at that offset."""
+    from specdec_nanovllm_b200 import workloads
+    draft, target, tokens = workloads.cfg4_inputs(B=8, k=6, V=4096, seed=21)
+    off = torch.tensor([5], dtype=torch.int64, device="cuda")
+    r = pkg.verify_batch(draft, target, tokens, None, seed=3, offset_tensor=off)
+    w = pkg.verify_batch(draft, target, tokens, None, seed=3, offset=5)
+    torch.cuda.synchronize()
+    assert torch.equal(r.accepted, w.accepted) and torch.equal(r.bonus, w.bonus)
+    assert torch.equal(r.accept_mask, w.accept_mask)
+    assert int(off.item()) == 6
+    g = torch.cuda.CUDAGraph()
+    st = torch.cuda.Stream()
+    st.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(st):
+        with torch.cuda.graph(g, stream=st):
+            pkg.verify_batch(draft, target, tokens, None, seed=3, offset_tensor=off, out=r)
+    torch.cuda.current_stream().wait_stream(st)
+    for v in (6, 7, 8):
+        g.replay()
+        torch.cuda.synchronize()
+        w = pkg.verify_batch(draft, target, tokens, None, seed=3, offset=v)
+        torch.cuda.synchronize()
+        assert torch.equal(r.accepted, w.accepted) and torch.equal(r.bonus, w.bonus), v
+    assert int(off.item()) == 9
+    del g
