@@ -286,6 +286,9 @@ int w8a16_umma_launch(const void* x, int64_t x_srow, const int8_t* w, const void
                       void* y, int64_t y_srow, int M, int N, int K, int act_dtype, float* part, int* err,
                       cudaStream_t st);
 bool w8a16_cluster_eligible(int M, int N, int K, int group, int act_dtype, bool require_balance);
+bool w8a16_gemv_eligible(int M, int N, int K, int group);
+int w8a16_gemv_launch(const void* x, int64_t x_srow, const int8_t* w, const void* s, int s_dtype, const void* bias,
+                      void* y, int64_t y_srow, int M, int N, int K, int act_dtype, cudaStream_t st);
 int w8a16_cluster_launch(const void* x, int64_t x_srow, const int8_t* w, const void* s, int s_dtype, const void* bias,
                          void* y, int64_t y_srow, int M, int N, int K, int act_dtype, int* err, cudaStream_t st);
 
@@ -321,13 +324,22 @@ static size_t umma_ws_bytes(int M, int N, int K) {
 // Kernel choice (per-channel scales, K % 128 == 0): for 17 to 128 tokens the cluster
 // split-K tcgen05 kernel (w8a16_cluster.cu) unless its plan leaves the busiest CTA 3 or
 // more units above an even split (then the stream-K kernel, w8a16_umma.cu); the stream-K
-// kernel above 128 tokens; the register kernel up to 16 tokens and for grouped scales.
+// kernel above 128 tokens.  Up to 16 tokens the weight-stream kernel (w8a16_gemv.cu) for
+// the shapes whose token rows fit its shared memory, at 13-16 tokens only up to 8192
+// features (above that the register kernel measured faster: gate_up at 16 tokens 25.4
+// against 28.8 us); the register kernel for the other shapes up to 16 tokens and for
+// grouped scales.
 // SDB_W8A16_KERNEL=cluster takes the cluster kernel wherever it has a plan, =umma skips it,
-// =mma forces the register kernel (read per call: tests switch it).
-enum class Kern { Cluster, Umma, Mma };
-static Kern choose(int M, int N, int K, int group, int act_dtype) {
+// =mma forces the register kernel, =gemv takes the weight-stream kernel wherever it has a
+// plan (read per call: tests switch it).
+enum class Kern { Cluster, Umma, Mma, Gemv };
+static Kern choose(int M, int N, int K, int group, int act_dtype, const void* w) {
     const char* e = getenv("SDB_W8A16_KERNEL");
     if (e && !strcmp(e, "mma")) return Kern::Mma;
+    const bool w32 = (reinterpret_cast<uintptr_t>(w) & 31) == 0;  // 256-bit weight loads
+    const bool gemv_ok = w32 && w8a16_gemv_eligible(M, N, K, group);
+    if (e && !strcmp(e, "gemv") && gemv_ok) return Kern::Gemv;
+    if (!e && gemv_ok && (M <= 12 || N <= 8192)) return Kern::Gemv;
     const bool no_cluster = e && !strcmp(e, "umma");
     const bool any_cluster = e && !strcmp(e, "cluster");
     if (!no_cluster && w8a16_cluster_eligible(M, N, K, group, act_dtype, !any_cluster)) return Kern::Cluster;
@@ -397,7 +409,9 @@ extern "C" int sdb_w8a16_linear(const void* x, int64_t x_srow, const int8_t* qwe
         return SDB_ERR_INVALID_ARG;
     }
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-    const w8::Kern kern = w8::choose(M, N, K, group_size, act_dtype);
+    const w8::Kern kern = w8::choose(M, N, K, group_size, act_dtype, qweight);
+    if (kern == w8::Kern::Gemv)
+        return w8a16_gemv_launch(x, x_srow, qweight, scale, scale_dtype, bias, y, y_srow, M, N, K, act_dtype, st);
     if (kern == w8::Kern::Cluster) {
         if (workspace_bytes < w8::kUmmaPartOffset) {
             set_last_error("workspace too small: need %zu bytes, got %zu", w8::kUmmaPartOffset, workspace_bytes);

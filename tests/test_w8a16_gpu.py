@@ -17,13 +17,16 @@ pytestmark = pytest.mark.gpu
 TOL = dict(rtol=2e-2, atol=2e-3)
 
 
-@pytest.fixture(autouse=True, params=["auto", "cluster", "umma", "mma"])
+@pytest.fixture(autouse=True, params=["auto", "cluster", "umma", "mma", "gemv"])
 def kernel_choice(request, monkeypatch):
-    """Every test runs on the default kernel (where the shape allows: the register kernel up
-    to 16 tokens, for 17 to 128 the cluster split-K tcgen05 kernel unless its plan is
-    unbalanced, else and above 128 the stream-K tcgen05 kernel), on the cluster kernel
+    """Every test runs on the default kernel (where the shape allows: the weight-stream kernel
+    up to 16 tokens, else the register kernel, for 17 to 128 the cluster split-K tcgen05
+    kernel unless its plan is unbalanced, else and above 128 the stream-K tcgen05 kernel),
+    on the cluster kernel
     wherever it has a plan (SDB_W8A16_KERNEL=cluster), on the stream-K kernel alone above 16
-    tokens (SDB_W8A16_KERNEL=umma) and on the register kernel (SDB_W8A16_KERNEL=mma)."""
+    tokens (SDB_W8A16_KERNEL=umma), on the register kernel (SDB_W8A16_KERNEL=mma) and on the
+    weight-stream kernel wherever it has a plan (SDB_W8A16_KERNEL=gemv: 1-16 tokens,
+    per-channel scales, K % 128 == 0, the tokens within its shared memory)."""
     if request.param == "auto":
         monkeypatch.delenv("SDB_W8A16_KERNEL", raising=False)
     else:
@@ -90,6 +93,25 @@ def test_cluster_split_shapes(pkg, M, N, K):
     s = (torch.rand(N, generator=g, device="cuda") * 0.01).to(torch.float16)
     x = torch.randn(M, K, generator=g, device="cuda").to(torch.float16)
     bias = torch.randn(N, generator=g, device="cuda").to(torch.float16)
+    y = pkg.int8_linear(x, q, s, bias)
+    torch.cuda.synchronize()
+    _check(y, _ref(x, q, s, bias))
+
+
+@pytest.mark.parametrize("M", [1, 3, 8, 9, 16])
+@pytest.mark.parametrize("N,K", [(7, 128), (203, 384), (1030, 1280), (2560, 9728), (19456, 2560)])
+def test_small_token_counts(pkg, M, N, K):
+    """1-16 tokens: fewer features than CTAs (7, 203), ragged tiles (1030 rows over the CTAs),
+    the down projection (9728-wide token rows: 16 tokens do not fit the weight-stream kernel's
+    shared memory and take the register kernel) and gate_up; one and two 8-token fragments,
+    f16 and bf16 activations, bias on odd token counts."""
+    g = torch.Generator(device="cuda").manual_seed(M * 31 + N + K)
+    dt = torch.bfloat16 if M in (3, 9) else torch.float16     # bf16 with one and two fragments
+    q = torch.randint(-127, 128, (N, K), generator=g, device="cuda", dtype=torch.int32).to(torch.int8)
+    s = torch.rand(N, generator=g, device="cuda") * 0.01
+    s = s if dt == torch.bfloat16 else s.to(torch.float16)    # float32 scales with bf16
+    x = torch.randn(M, K, generator=g, device="cuda").to(dt)
+    bias = torch.randn(N, generator=g, device="cuda").to(dt) if M % 2 else None
     y = pkg.int8_linear(x, q, s, bias)
     torch.cuda.synchronize()
     _check(y, _ref(x, q, s, bias))
