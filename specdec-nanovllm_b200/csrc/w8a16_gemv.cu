@@ -55,12 +55,17 @@ struct Params {
     int part_bytes;  // shared-memory bytes of the warps' partial sums
 };
 
-// 32 contiguous weight bytes, not kept in L1; the L2 fetch is promoted to 256 bytes (the
-// warp reads the following 128 bytes of each row with its next block).
-SDB_DEV void ldg256(const int8_t* p, uint32_t (&r)[8]) {
-    asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
-                 : "l"(p));
+// 32 contiguous weight bytes if `ok` (else r holds stale bits: int8 data of some earlier
+// block or zeros, which convert to finite values that only reach accumulator rows of
+// missing weight rows or blocks that are never consumed), not kept in L1; the L2 fetch is
+// promoted to 256 bytes (the warp reads the following 128 bytes of each row with its next
+// block).  Predicated inside the instruction, so the call site has no branch.
+SDB_DEV void ldg256(const int8_t* p, bool ok, uint32_t (&r)[8]) {
+    asm volatile(
+        "{\n.reg .pred q;\nsetp.ne.b32 q, %9, 0;\n"
+        "@q ld.global.nc.L1::no_allocate.L2::256B.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n}"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+        : "l"(p), "r"((int)ok));
 }
 
 SDB_DEV void cp_async16(uint32_t dst, const void* src) {
@@ -89,10 +94,10 @@ SDB_DEV void cursor_tile(Cursor& c, const Params& p, int r0, int R, int T, int g
     c.p1 = c.p0 + (int64_t)8 * p.K;
 }
 
-SDB_DEV void load_block(Cursor& c, const Params& p, int r0, int R, int T, int g, int t4, uint32_t (&a)[8],
+SDB_DEV void load_block(Cursor& c, bool go, const Params& p, int r0, int R, int T, int g, int t4, uint32_t (&a)[8],
                         uint32_t (&b)[8]) {
-    if (c.ok0) ldg256(c.p0, a);
-    if (c.ok1) ldg256(c.p1, b);
+    ldg256(c.p0, go && c.ok0, a);
+    ldg256(c.p1, go && c.ok1, b);
     c.p0 += KBLK;
     c.p1 += KBLK;
     if (++c.b == p.kb) {
@@ -128,8 +133,7 @@ __global__ void __launch_bounds__(WARPS * 32, MINB) w8a16_gemv_kernel(const Para
     lc.b = u0 - lc.t * p.kb;
     cursor_tile(lc, p, r0, R, T, g, t4);
 #pragma unroll
-    for (int i = 0; i < S; ++i)
-        if (u0 + i < u1) load_block(lc, p, r0, R, T, g, t4, ra[i], rb[i]);
+    for (int i = 0; i < S; ++i) load_block(lc, u0 + i < u1, p, r0, R, T, g, t4, ra[i], rb[i]);
     // per-channel scales and bias of the CTA's rows (constant: read before the wait too)
     float* sc = reinterpret_cast<float*>(smem + p.x_bytes + p.part_bytes);
     for (int r = threadIdx.x; r < R; r += WARPS * 32) {
@@ -171,10 +175,6 @@ __global__ void __launch_bounds__(WARPS * 32, MINB) w8a16_gemv_kernel(const Para
         for (int i = 0; i < S; ++i) {
             const int u = base + i;
             if (u >= u1) break;
-            // refill the slot the previous unit used with the unit D ahead (the first S
-            // units were loaded before the wait)
-            if (u > u0 && u + D < u1)
-                load_block(lc, p, r0, R, T, g, t4, ra[(i + D) % S], rb[(i + D) % S]);
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
                 uint32_t xw[16];
@@ -200,6 +200,8 @@ __global__ void __launch_bounds__(WARPS * 32, MINB) w8a16_gemv_kernel(const Para
                 }
                 xp[nt] += 256;
             }
+            // the slot is converted: refill it with the unit S ahead (D others stay in flight)
+            load_block(lc, u + S < u1, p, r0, R, T, g, t4, ra[i], rb[i]);
             if (++cb == p.kb) {  // tile done: partial sums to shared memory
                 float* pp = part + ((warp * p.J + jt) * NT) * 128;
 #pragma unroll
@@ -247,7 +249,7 @@ __global__ void __launch_bounds__(WARPS * 32, MINB) w8a16_gemv_kernel(const Para
 }
 
 constexpr int kWarps = 8;
-constexpr int kDepth1 = 4, kDepth2 = 3;    // weight blocks in flight per warp (1 / 2 token fragments)
+constexpr int kDepth1 = 4, kDepth2 = 2;    // weight blocks in flight per warp (1 / 2 token fragments)
 constexpr int kCtasPerSm = 2;              // register budget of the launch bounds
 constexpr size_t kSmemCap = 200 * 1024;
 constexpr size_t kSmemPerSm = 228 * 1024;  // shared memory of one SM (1 KB reserved per CTA)
