@@ -568,9 +568,13 @@ def run_specdec_e2e(args):
     from specdec_nanovllm_b200.partition import shard_range
     from specdec_nanovllm_b200.specdec import QWEN3_06B, QWEN3_4B, RandomQwen3, SpecDecodeStep
     Bg, ctx, k = args.global_batch, 2048, K_SPEC
-    lo, hi = shard_range(Bg, world, rank)
-    target = RandomQwen3(QWEN3_4B, dev, seed=1)
-    draft = RandomQwen3(QWEN3_06B, dev, seed=2)
+    tp = world if args.tp else 1
+    # sequence sharding: each rank its share of the batch; tensor parallel: every rank all
+    # of it, with the rank's slice of both models
+    lo, hi = shard_range(Bg, world, rank) if tp == 1 else (0, Bg)
+    group = dist.group.WORLD if tp > 1 else None
+    target = RandomQwen3(QWEN3_4B, dev, seed=1, tp_rank=rank if tp > 1 else 0, tp_size=tp, group=group)
+    draft = RandomQwen3(QWEN3_06B, dev, seed=2, tp_rank=rank if tp > 1 else 0, tp_size=tp, group=group)
     st = SpecDecodeStep(target, draft, hi - lo, ctx, k, dev, seed=100 + lo)
     st.prepare()
     steps = max(1, min(args.steps, 50))
@@ -614,7 +618,7 @@ def run_specdec_e2e(args):
         sm = stats.clone()
         dist.all_reduce(sm, op=dist.ReduceOp.SUM)
         ms, t_draft, t_target, t_verify = float(mx[0]), float(mx[2]), float(mx[3]), float(mx[4])
-        tokens = float(sm[1])
+        tokens = float(sm[1]) if tp == 1 else float(stats[1])   # TP: every rank commits the same tokens
     tok_s = tokens / (ms * 1e-3)
     if rank == 0:
         line = {"metric": "spec-decode tok/s, Qwen3-4B target + Qwen3-0.6B draft, k=6", "value": round(tok_s, 1),
@@ -622,7 +626,8 @@ def run_specdec_e2e(args):
                 "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
                 "dtype": "bf16", "data": "synthetic (random-init weights, N(0,1) KV context)",
                 "config": {"workload": f"spec decode step, {Bg} sequences x {ctx} context, k={k}, CUDA graphs",
-                           "global_batch": Bg, "seq_len": ctx, "k": k, "parallelism": f"seq-shard{world}"},
+                           "global_batch": Bg, "seq_len": ctx, "k": k,
+                           "parallelism": f"tp{world}" if tp > 1 else f"seq-shard{world}"},
                 "tokens_per_step": round(tokens, 2),
                 "mean_accepted_per_seq": round(tokens / Bg - 1.0, 3),
                 "phases_ms": {"draft_k_steps": round(t_draft, 3),
@@ -834,6 +839,9 @@ def main():
                     default="verify_attn", help="verify_attn is the headline; the others measure the "
                     "secondary kernels of the path on one GPU")
     ap.add_argument("--m", type=int, default=1, help="tokens (M) for --mode w8a16")
+    ap.add_argument("--tp", action="store_true",
+                    help="--mode specdec_e2e under torchrun: tensor-parallel models over the ranks "
+                         "(all-reduce after o_proj / down_proj) instead of sharded sequences")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.impl == "reference":

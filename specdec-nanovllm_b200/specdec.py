@@ -27,6 +27,15 @@ kept on the device, which each call reads and advances, so every replay draws an
 Models are random-init (there are no checkpoints): weights N(0, 0.02) in bf16, norm
 weights 1, tied embeddings.  The KV caches start filled with N(0, 1) values standing for
 a ``context``-token prefix, so a step runs at that context without a prefill.
+
+Tensor parallel (``tp_size`` > 1, one rank per GPU): the Megatron split of the reference's
+``linear.py:68-170`` -- q/k/v heads and the gate/up rows column-parallel, o_proj and
+down_proj row-parallel followed by an NCCL all-reduce of their (tokens, hidden) partial
+sums (``RowParallelLinear.forward``, :165-170), the KV cache holding the rank's kv heads.
+The embedding and the tied LM head are replicated rather than vocab-parallel, so every
+rank holds the same logits and runs the same sampler and ``verify_batch`` draws: no
+collective besides the two all-reduces per layer.  Each rank's slices are cut from the
+same full weights a single-device model with the same seed holds.
 """
 
 from __future__ import annotations
@@ -35,6 +44,7 @@ import math
 from dataclasses import dataclass
 
 import torch
+import torch.distributed as dist
 import torch.nn.functional as F
 
 from .attention import paged_attention
@@ -71,60 +81,98 @@ def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float, residual: torch.Tenso
 
 
 class RandomQwen3:
-    """A Qwen3 decoder with random bf16 weights, run on the package's kernels."""
+    """A Qwen3 decoder with random bf16 weights, run on the package's kernels; with
+    ``tp_size`` > 1 the rank's tensor-parallel slice of it (all-reduce over ``group``)."""
 
     def __init__(self, shape: Qwen3Shape, device, seed: int, max_position: int = 8192,
-                 dtype=torch.bfloat16):
+                 dtype=torch.bfloat16, tp_rank: int = 0, tp_size: int = 1, group=None):
+        if shape.heads % tp_size or shape.kv_heads % tp_size or shape.ffn % tp_size:
+            raise ValueError(f"tp_size {tp_size} must divide heads {shape.heads}, kv heads "
+                             f"{shape.kv_heads} and ffn {shape.ffn}")
         self.s = shape
         self.dtype = dtype
+        self.tp_rank, self.tp_size, self.group = tp_rank, tp_size, group
+        self.heads, self.kv_heads = shape.heads // tp_size, shape.kv_heads // tp_size
         g = torch.Generator(device=device).manual_seed(seed)
-        H, D = shape.hidden, shape.head_dim
+        H, D, F_ = shape.hidden, shape.head_dim, shape.ffn
+        r, hq, hk, fl = tp_rank, self.heads * D, self.kv_heads * D, F_ // tp_size
 
         def w(out_f, in_f):
             return (torch.randn(out_f, in_f, generator=g, device=device, dtype=torch.float32) * 0.02).to(dtype)
 
+        def rows(t, *ranges):          # the rank's row ranges of a full weight, concatenated
+            return torch.cat([t[a:b] for a, b in ranges]).contiguous()
+
         self.embed = w(shape.vocab, H)          # tied with the LM head
         self.layers = []
         for _ in range(shape.layers):
+            qkv, o, gate_up, down = (w((shape.heads + 2 * shape.kv_heads) * D, H), w(H, shape.heads * D),
+                                     w(2 * F_, H), w(H, F_))
+            q0, k0, v0 = 0, shape.heads * D, (shape.heads + shape.kv_heads) * D
             self.layers.append(dict(
                 ln1=torch.ones(H, device=device, dtype=dtype),
                 ln2=torch.ones(H, device=device, dtype=dtype),
-                qkv=w((shape.heads + 2 * shape.kv_heads) * D, H),
+                qkv=rows(qkv, (q0 + r * hq, q0 + (r + 1) * hq), (k0 + r * hk, k0 + (r + 1) * hk),
+                         (v0 + r * hk, v0 + (r + 1) * hk)),
                 q_norm=torch.ones(D, device=device, dtype=dtype),
                 k_norm=torch.ones(D, device=device, dtype=dtype),
-                o=w(H, shape.heads * D),
-                gate_up=w(2 * shape.ffn, H),
-                down=w(H, shape.ffn)))
+                o=o[:, r * hq:(r + 1) * hq].contiguous(),
+                gate_up=rows(gate_up, (r * fl, (r + 1) * fl), (F_ + r * fl, F_ + (r + 1) * fl)),
+                down=down[:, r * fl:(r + 1) * fl].contiguous()))
+            del qkv, o, gate_up, down
         self.norm = torch.ones(H, device=device, dtype=dtype)
         self.cos_sin = rope_cos_sin_cache(D, max_position, shape.rope_theta, device=device)
         self.scale = 1.0 / math.sqrt(D)
 
     def new_cache(self, num_blocks: int, page: int, device, seed: int):
-        """Per layer (num_blocks, page, Hkv, D) K and V caches, filled with N(0, 1)."""
+        """Per layer (num_blocks, page, Hkv / tp, D) K and V caches: the rank's kv heads of
+        full caches filled with N(0, 1)."""
         g = torch.Generator(device=device).manual_seed(seed)
         shp = (num_blocks, page, self.s.kv_heads, self.s.head_dim)
-        return [(torch.randn(shp, generator=g, device=device, dtype=self.dtype),
-                 torch.randn(shp, generator=g, device=device, dtype=self.dtype)) for _ in range(self.s.layers)]
+        h0, h1 = self.tp_rank * self.kv_heads, (self.tp_rank + 1) * self.kv_heads
+        out = []
+        for _ in range(self.s.layers):
+            kv = []
+            for _ in range(2):
+                full = torch.randn(shp, generator=g, device=device, dtype=self.dtype)
+                kv.append(full if self.tp_size == 1 else full[:, :, h0:h1].contiguous())
+                del full
+            out.append(tuple(kv))
+        return out
 
-    def forward(self, ids, positions, slots, block_tables, seqlens, n_q: int, cache) -> torch.Tensor:
-        """Hidden states (T, H) of T = B * n_q tokens, rows b * n_q .. b * n_q + n_q - 1 of
-        sequence b at consecutive positions ending at seqlens[b] - 1 (decode: n_q = 1)."""
+    def forward_steps(self, ids, positions, slots, block_tables, seqlens, n_q: int, cache):
+        """The forward as a generator: it yields the (T, H) partial sums of o_proj and of
+        down_proj and resumes with their sums over the tensor-parallel ranks; it returns the
+        final hidden states.  ``forward`` drives it with an NCCL all-reduce."""
         s = self.s
         h = F.embedding(ids, self.embed)
         residual = None
         for lw, (kc, vc) in zip(self.layers, cache):
             x, residual = rms_norm(h, lw["ln1"], s.eps, residual)
             qkv = F.linear(x, lw["qkv"])
-            q = qk_norm_rope_store(qkv, positions, s.heads, s.kv_heads, s.head_dim, self.cos_sin,
+            q = qk_norm_rope_store(qkv, positions, self.heads, self.kv_heads, s.head_dim, self.cos_sin,
                                    lw["q_norm"], lw["k_norm"], s.eps, k_cache=kc, v_cache=vc,
                                    slot_mapping=slots)
             o = paged_attention(q, kc, vc, block_tables, seqlens, self.scale, n_q=n_q)
-            h = F.linear(o.view(o.shape[0], -1), lw["o"])
+            h = yield F.linear(o.view(o.shape[0], -1), lw["o"])
             x, residual = rms_norm(h, lw["ln2"], s.eps, residual)
             gu = F.linear(x, lw["gate_up"])
-            h = F.linear(silu_and_mul(gu), lw["down"])
+            h = yield F.linear(silu_and_mul(gu), lw["down"])
         h, _ = rms_norm(h, self.norm, s.eps, residual)
         return h
+
+    def forward(self, ids, positions, slots, block_tables, seqlens, n_q: int, cache) -> torch.Tensor:
+        """Hidden states (T, H) of T = B * n_q tokens, rows b * n_q .. b * n_q + n_q - 1 of
+        sequence b at consecutive positions ending at seqlens[b] - 1 (decode: n_q = 1)."""
+        steps = self.forward_steps(ids, positions, slots, block_tables, seqlens, n_q, cache)
+        part = next(steps)
+        while True:
+            if self.tp_size > 1:
+                dist.all_reduce(part, group=self.group)
+            try:
+                part = steps.send(part)
+            except StopIteration as done:
+                return done.value
 
     def logits(self, h: torch.Tensor) -> torch.Tensor:
         return F.linear(h, self.embed)

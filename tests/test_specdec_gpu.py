@@ -112,3 +112,51 @@ def test_spec_decode_step_matches_float32_model_and_graph_replay(pkg):
         assert st.cands.min() >= 0 and st.cands.max() < tshape.vocab
         assert torch.isfinite(st.draft_logits).all()
     st.close()
+
+
+@pytest.mark.parametrize("tp", [2])
+def test_tensor_parallel_slices_reduce_to_single_device_forward(pkg, tp):
+    """`tp` tensor-parallel slices of the target (heads and FFN columns split, o_proj /
+    down_proj partial sums added as the NCCL all-reduce adds them, in bf16) driven in
+    lockstep on one GPU through `forward_steps`: every rank ends with the same hidden states,
+    and they match the single-device forward of the same model within bf16 tolerance; the
+    ranks' KV caches hold their heads of the single-device cache."""
+    from specdec_nanovllm_b200.specdec import RandomQwen3, SpecDecodeStep
+    dev = torch.device("cuda")
+    tshape, dshape = _shapes(pkg)
+    full = RandomQwen3(tshape, dev, seed=1, max_position=1024)
+    draft = RandomQwen3(dshape, dev, seed=2, max_position=1024)
+    B, ctx, k = 3, 300, 3
+    st = SpecDecodeStep(full, draft, B, ctx, k, dev, seed=5, use_graphs=False)
+    nb = st.t_cache[0][0].shape[0]
+    shards = [RandomQwen3(tshape, dev, seed=1, max_position=1024, tp_rank=r, tp_size=tp) for r in range(tp)]
+    caches = [m.new_cache(nb, st.page, dev, 5 + 1) for m in shards]      # SpecDecodeStep's target seed
+    hk = tshape.kv_heads // tp
+    for r, c in enumerate(caches):
+        assert torch.equal(c[1][0], st.t_cache[1][0][:, :, r * hk:(r + 1) * hk])
+    ids = torch.randint(0, tshape.vocab, (B * (k + 1),), generator=torch.Generator().manual_seed(3)).to(dev)
+    want = full.forward(ids, st.v_pos, st.v_slots, st.block_tables, st.v_lens, k + 1, st.t_cache)
+    gens = [m.forward_steps(ids, st.v_pos, st.v_slots, st.block_tables, st.v_lens, k + 1, c)
+            for m, c in zip(shards, caches)]
+    parts, outs = [next(g) for g in gens], []
+    while not outs:
+        total = parts[0]
+        for p in parts[1:]:
+            total = total + p                          # bf16 sums, as the all-reduce makes them
+        nxt = []
+        for g in gens:
+            try:
+                nxt.append(g.send(total.clone()))
+            except StopIteration as done:
+                outs.append(done.value)
+        parts = nxt
+    assert len(outs) == tp and all(torch.equal(o, outs[0]) for o in outs[1:])
+    got, ref = outs[0].float(), want.float()
+    cos = F.cosine_similarity(got.flatten(), ref.flatten(), dim=0).item()
+    err = (got - ref).abs().max().item()
+    assert cos > 0.999 and err < 0.05 * ref.abs().max().item(), (cos, err)
+    for r, c in enumerate(caches):                    # the verify rows were stored in every shard
+        new = st.v_slots.long()
+        kr = c[0][0].view(-1, hk, tshape.head_dim)[new].float()
+        kf = st.t_cache[0][0].view(-1, tshape.kv_heads, tshape.head_dim)[new][:, r * hk:(r + 1) * hk].float()
+        assert F.cosine_similarity(kr.flatten(), kf.flatten(), dim=0).item() > 0.999
