@@ -134,11 +134,15 @@ __global__ void __launch_bounds__(WARPS * 32, MINB) w8a16_gemv_kernel(const Para
     cursor_tile(lc, p, r0, R, T, g, t4);
 #pragma unroll
     for (int i = 0; i < S; ++i) load_block(lc, u0 + i < u1, p, r0, R, T, g, t4, ra[i], rb[i]);
-    // per-channel scales and bias of the CTA's rows (constant: read before the wait too)
+    // per-channel scales and bias of the CTA's rows (constant: the first WARPS * 32 are read
+    // into registers before the wait and stored to shared memory after it, so no thread
+    // waits for them on its way to the wait)
     float* sc = reinterpret_cast<float*>(smem + p.x_bytes + p.part_bytes);
-    for (int r = threadIdx.x; r < R; r += WARPS * 32) {
-        sc[r] = w8cv::scale_value(p.s, p.s_dtype, r0 + r);
-        sc[R + r] = p.bias ? to_f32(reinterpret_cast<const E*>(p.bias)[r0 + r]) : 0.f;
+    const E* bias = reinterpret_cast<const E*>(p.bias);
+    float s_first = 0.f, b_first = 0.f;
+    if ((int)threadIdx.x < R) {
+        s_first = w8cv::scale_value(p.s, p.s_dtype, r0 + threadIdx.x);
+        if (bias) b_first = to_f32(bias[r0 + threadIdx.x]);
     }
 
     pdl_wait();
@@ -149,6 +153,14 @@ __global__ void __launch_bounds__(WARPS * 32, MINB) w8a16_gemv_kernel(const Para
         for (int i = threadIdx.x; i < p.M * upr; i += WARPS * 32) {
             const int n = i / upr, u = i - n * upr;
             cp_async16(sbase + (uint32_t)(n * p.K * 2 + u * 16), xg + (int64_t)n * p.x_srow + u * 8);
+        }
+        if ((int)threadIdx.x < R) {
+            sc[threadIdx.x] = s_first;
+            sc[R + threadIdx.x] = b_first;
+        }
+        for (int r = threadIdx.x + WARPS * 32; r < R; r += WARPS * 32) {
+            sc[r] = w8cv::scale_value(p.s, p.s_dtype, r0 + r);
+            sc[R + r] = bias ? to_f32(bias[r0 + r]) : 0.f;
         }
         asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
     }
