@@ -774,6 +774,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (!ok && lane == 0) atomicOr(p.err, SDB_KERR_TIMEOUT);
     }
 
+    // each warp reconverges first (the producer, MMA and idle lanes of warps 0, 1 and the
+    // P.V warp come from different branches), so the block barrier below holds every thread
+    // until the softmax warps' last TMEM reads are done
+    __syncwarp();
     tc_fence_before();
     __syncthreads();
     tc_fence_after();

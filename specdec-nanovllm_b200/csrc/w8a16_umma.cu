@@ -301,6 +301,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         if (!ok && lane == 0) atomicOr(p.err, SDB_KERR_TIMEOUT);
     }
+    __syncwarp();  // warps reconverge (role lanes and idle lanes) before the block barrier
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
