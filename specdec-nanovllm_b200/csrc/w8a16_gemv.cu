@@ -55,11 +55,12 @@ struct Params {
     int part_bytes;  // shared-memory bytes of the warps' partial sums
 };
 
-// 32 contiguous weight bytes if `ok` (else r holds stale bits: int8 data of some earlier
-// block or zeros, which convert to finite values that only reach accumulator rows of
-// missing weight rows or blocks that are never consumed), not kept in L1; the L2 fetch is
-// promoted to 256 bytes (the warp reads the following 128 bytes of each row with its next
-// block).  Predicated inside the instruction, so the call site has no branch.
+// 32 contiguous weight bytes if `ok`, not kept in L1; the L2 fetch is promoted to 256
+// bytes (the warp reads the following 128 bytes of each row with its next block).
+// Predicated inside the instruction, so the call site has no branch.  If `ok` is false, r
+// keeps whatever bits its registers held: every 32-bit pattern converts to four finite
+// int8 values, and they only reach accumulator rows of missing weight rows, or blocks past
+// the warp's range that are never consumed.
 SDB_DEV void ldg256(const int8_t* p, bool ok, uint32_t (&r)[8]) {
     asm volatile(
         "{\n.reg .pred q;\nsetp.ne.b32 q, %9, 0;\n"
@@ -122,7 +123,7 @@ __global__ void __launch_bounds__(WARPS * 32, MINB) w8a16_gemv_kernel(const Para
     const int U = T * p.kb;
     const int u0 = (int)((int64_t)warp * U / WARPS), u1 = (int)((int64_t)(warp + 1) * U / WARPS);
 
-    // first D weight blocks: independent of the preceding kernel
+    // the first S = D + 1 weight blocks: independent of the preceding kernel
     uint32_t ra[S][8], rb[S][8];
 #pragma unroll
     for (int i = 0; i < S; ++i)
